@@ -1,0 +1,109 @@
+"""ctypes binding of libapa_kernels.so (declared in include/apa_kernels.h).
+
+The library is the only compute path of this package: there is no CPU or
+torch-op fallback. Loading it needs no GPU; calling into it does. A missing
+library, or any nonzero status from an entry point, raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libapa_kernels.so")
+
+OK, ERR_INVALID, ERR_ALIGN, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3, 4
+DT_F32, DT_F16, DT_BF16, DT_E4M3 = 0, 1, 2, 3
+RUNG_FP8, RUNG_FP16, RUNG_TF32 = 0, 1, 2
+EPI_FWD, EPI_DGRAD, EPI_WGRAD = 0, 1, 2
+
+_VP = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+
+# name -> argtypes (all entry points return int status unless noted)
+SIGNATURES = {
+    "apa_abi_version": [],
+    "apa_status_string": [_I],
+    "apa_get_device_status": [_VP, _I],
+    "apa_cast": [_VP, _I, _I64, _I64, _I64, _VP, _I, _I64, _VP, _I64, _VP, _VP, _I, _VP, _VP, _VP],
+    "apa_amax": [_VP, _I, _I64, _VP, _VP, _VP],
+    "apa_underflow_ratio": [_VP, _I, _I64, ctypes.c_float, _VP, _VP, _I, _VP],
+    "apa_merge_telemetry": [_VP, _VP, _VP, _VP],
+    "apa_colsum_finalize": [_VP, _I64, _I64, _I, _VP, _I, _VP],
+    "apa_zero_list": [_VP, _I, _VP],
+    "apa_linear_fwd": [_I, _VP, _I64, _VP, _I64, _VP, _VP, _I64, _I64, _I64, _I64, _VP, _VP, _VP],
+    "apa_linear_dgrad": [_I, _VP, _I64, _VP, _I64, _VP, _I, _I64, _I64, _I64, _I64, _VP, _VP, _VP],
+    "apa_linear_wgrad": [_I, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _I64, _I, _VP, _VP, _VP],
+    "apa_gemm_tn": [_I, _I, _VP, _I64, _VP, _I64, _VP, _I, _I64, _I64, _I64, _I64, _I, _I, _VP],
+    "apa_ladder_pack": [_I, _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP],
+    "apa_ladder_eval": [_I, _VP, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _I64, _I64,
+                        ctypes.c_double, ctypes.c_double, _VP, _VP],
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class APAKernelError(RuntimeError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the kernel library."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise ImportError(
+                        f"{LIB_PATH} is missing: build it with "
+                        "`python adaptive-precision-ascension_b200/build.py` (nvcc, sm_100a)")
+                handle = ctypes.CDLL(LIB_PATH)
+                for name, args in SIGNATURES.items():
+                    fn = getattr(handle, name)
+                    fn.argtypes = args
+                    fn.restype = ctypes.c_char_p if name == "apa_status_string" else ctypes.c_int
+                _lib = handle
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != OK:
+        msg = lib().apa_status_string(status).decode()
+        raise APAKernelError(f"{what} failed: status {status} ({msg})")
+
+
+def ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_handle(device=None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+_DT = {torch.float32: DT_F32, torch.float16: DT_F16, torch.bfloat16: DT_BF16}
+if hasattr(torch, "float8_e4m3fn"):
+    _DT[torch.float8_e4m3fn] = DT_E4M3
+
+
+def dt_code(dtype: torch.dtype) -> int:
+    try:
+        return _DT[dtype]
+    except KeyError:
+        raise APAKernelError(f"dtype {dtype} is not supported by the APA kernels") from None
+
+
+def require_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise APAKernelError(
+            f"{what}: tensor on {t.device}; the APA kernels run only on CUDA (sm_100a) devices")
+
+
+def device_status(clear: bool = True) -> int:
+    out = ctypes.c_uint(0)
+    check(lib().apa_get_device_status(ctypes.byref(out), 1 if clear else 0), "apa_get_device_status")
+    return out.value

@@ -1,0 +1,134 @@
+"""Data-parallel gradient averaging for APAManager.
+
+The reference has no gradient synchronisation at all (its only collective is
+the overflow flag, manager.py:186-187). Data parallel training here averages
+every trainable gradient across ranks once per step. Gradients are grouped
+into flat fp32 buckets (in reverse registration order, roughly the order the
+backward produces them); each parameter's ``.grad`` is a view into its
+bucket, so the weight-gradient kernels and autograd write straight into the
+buffers that NCCL reduces, with no packing copies. A bucket's all-reduce is
+issued (asynchronously, on the process group's stream) as soon as all of its
+gradients are written, and buckets are issued in a fixed order so every rank
+runs the same collectives in the same sequence.
+"""
+from __future__ import annotations
+
+from typing import Dict, List
+
+import torch
+import torch.distributed as dist
+
+
+class _Bucket:
+    def __init__(self, params: List[torch.nn.Parameter], device):
+        self.params = params
+        self.numel = sum(p.numel() for p in params)
+        self.flat = torch.zeros(self.numel, dtype=torch.float32, device=device)
+        self.views: Dict[int, torch.Tensor] = {}
+        off = 0
+        for p in params:
+            self.views[id(p)] = self.flat[off:off + p.numel()].view_as(p)
+            off += p.numel()
+        self.pending = len(params)
+        self.handle = None
+
+
+class GradientAverager:
+    def __init__(self, mgr, process_group=None, bucket_bytes: int = 64 << 20):
+        self.pg = process_group
+        self.world = dist.get_world_size(process_group)
+        self.avg_op = dist.ReduceOp.AVG if dist.get_backend(process_group) == "nccl" else None
+        params = [p for p in mgr.get_trainable_parameters() if p.dtype == torch.float32]
+        params = list(reversed(params))
+        device = params[0].device if params else torch.device("cpu")
+        self.buckets: List[_Bucket] = []
+        cur, cur_bytes = [], 0
+        for p in params:
+            cur.append(p)
+            cur_bytes += p.numel() * 4
+            if cur_bytes >= bucket_bytes:
+                self.buckets.append(_Bucket(cur, device))
+                cur, cur_bytes = [], 0
+        if cur:
+            self.buckets.append(_Bucket(cur, device))
+        self.where = {}
+        for bi, b in enumerate(self.buckets):
+            for p in b.params:
+                self.where[id(p)] = bi
+        self.next = 0
+        self.armed = False
+        apa_params = set()
+        for m in mgr.apa_modules.values():
+            m._grad_ready_cb = self._apa_ready
+            apa_params.add(id(m.weight_master))
+            if m.bias_master is not None:
+                apa_params.add(id(m.bias_master))
+        self._hooks = []
+        for b in self.buckets:
+            for p in b.params:
+                if id(p) not in apa_params:
+                    self._hooks.append(p.register_post_accumulate_grad_hook(self._param_ready))
+
+    # grads are views into the buckets; re-attach after zero_grad(set_to_none)
+    def arm(self):
+        for b in self.buckets:
+            b.flat.zero_()
+            for p in b.params:
+                v = b.views[id(p)]
+                if p.grad is None or p.grad.data_ptr() != v.data_ptr():
+                    p.grad = v
+            b.pending = len(b.params)
+            b.handle = None
+        self.next = 0
+        self.armed = True
+
+    def _mark(self, p):
+        bi = self.where.get(id(p))
+        if bi is None or not self.armed:
+            return
+        b = self.buckets[bi]
+        b.pending -= 1
+        self._launch_ready()
+
+    def _apa_ready(self, mod):
+        self._mark(mod.weight_master)
+        if mod.bias_master is not None and mod.bias_master.requires_grad:
+            self._mark(mod.bias_master)
+
+    def _param_ready(self, p):
+        self._mark(p)
+
+    def _launch(self, b: _Bucket):
+        if self.avg_op is not None:
+            b.handle = dist.all_reduce(b.flat, op=self.avg_op, group=self.pg, async_op=True)
+        else:
+            b.handle = dist.all_reduce(b.flat, op=dist.ReduceOp.SUM, group=self.pg, async_op=True)
+
+    def _launch_ready(self):
+        while self.next < len(self.buckets) and self.buckets[self.next].pending <= 0:
+            self._launch(self.buckets[self.next])
+            self.next += 1
+
+    def finish(self):
+        """Issue every bucket not yet issued (in order) and make the current
+        stream wait for all of them; average when the backend has no AVG."""
+        while self.next < len(self.buckets):
+            self._launch(self.buckets[self.next])
+            self.next += 1
+        for b in self.buckets:
+            if b.handle is not None:
+                b.handle.wait()
+            if self.avg_op is None:
+                b.flat.div_(self.world)
+            for p in b.params:
+                v = b.views[id(p)]
+                if p.grad is None:
+                    p.grad = v
+                elif p.grad.data_ptr() != v.data_ptr():
+                    # the gradient was produced outside the bucket: reduce it separately
+                    if self.avg_op is not None:
+                        dist.all_reduce(p.grad, op=self.avg_op, group=self.pg)
+                    else:
+                        dist.all_reduce(p.grad, op=dist.ReduceOp.SUM, group=self.pg)
+                        p.grad.div_(self.world)
+        self.armed = False

@@ -1,0 +1,128 @@
+// Shared device helpers for the APA kernels (sm_100a only).
+//
+// Element conversions reproduce what torch does for the reference's casts
+// (apa/layers.py:17-21 boundary cast, :370-372 working copy, and the autograd
+// engine's re-casts of returned gradients). They are written from the format
+// definitions (OCP FP8 E4M3, IEEE-754 binary16/bfloat16), not from any
+// library's implementation.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+#include "../../include/apa_kernels.h"
+
+namespace apa {
+
+// ---------------------------------------------------------------------------
+// Status word shared by all kernels of the library: a bounded wait that gives
+// up, or a launch that sees an impossible configuration, ORs a bit in here and
+// returns instead of trapping. The host reads it with apa_get_device_status().
+// ---------------------------------------------------------------------------
+__device__ unsigned int g_status = 0;   // library is one translation unit
+
+constexpr unsigned int kStatusTimeoutFull = 1u << 0;   // MMA waited too long for a TMA stage
+constexpr unsigned int kStatusTimeoutEmpty = 1u << 1;  // producer waited too long for a free stage
+constexpr unsigned int kStatusTimeoutAcc = 1u << 2;    // accumulator hand-off timed out
+constexpr unsigned int kStatusBadConfig = 1u << 3;
+
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;   // 2 s
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---------------------------------------------------------------------------
+// E4M3 (float8_e4m3fn): bias 7, 3 mantissa bits, no infinities, S.1111.111 is
+// NaN, largest finite 448. torch's conversion is non-saturating: the rounded
+// magnitude 480 does not exist, so |x| > 464 (the midpoint between 448 and
+// 480) and any Inf/NaN encode as NaN with the input's sign.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t e4m3_from_f32(float f) {
+  const uint32_t u = __float_as_uint(f);
+  const uint32_t s = (u >> 24) & 0x80u;
+  const uint32_t a = u & 0x7FFFFFFFu;
+  if (a > 0x43E80000u) return s | 0x7Fu;          // > 464.0f, Inf or NaN
+  if (a < 0x3C800000u) {                          // below 2^-6: one quantum 2^-9
+    const float v = __uint_as_float(a) * 512.0f;  // exact power-of-two scaling
+    return s | __float2uint_rn(v);                // round half to even; 8 encodes 2^-6
+  }
+  // normal range: keep sign-less exponent + 3 mantissa bits, round half to even
+  uint32_t keep = a >> 20;
+  const uint32_t rem = a & 0xFFFFFu;
+  if (rem > 0x80000u || (rem == 0x80000u && (keep & 1u))) keep += 1u;
+  return s | (keep - (120u << 3));                // re-bias exponent 127 -> 7
+}
+
+__device__ __forceinline__ float e4m3_to_f32(uint32_t b) {
+  const uint32_t s = (b & 0x80u) << 24;
+  const uint32_t e = (b >> 3) & 0xFu, m = b & 7u;
+  if ((b & 0x7Fu) == 0x7Fu) return __uint_as_float(s | 0x7FC00000u);
+  if (e == 0) return __uint_as_float(s | __float_as_uint((float)m * 0.001953125f));
+  return __uint_as_float(s | ((e + 120u) << 23) | (m << 20));
+}
+
+// magnitude of an E4M3 code as fp32 bits (NaN sorts above every finite value)
+__device__ __forceinline__ uint32_t e4m3_mag_bits(uint32_t b) {
+  return __float_as_uint(e4m3_to_f32(b & 0x7Fu));
+}
+
+// ---------------------------------------------------------------------------
+// binary16: IEEE round-to-nearest-even, overflow to +-Inf. A NaN keeps its sign
+// and the top ten payload bits with the quiet bit set (torch's vectorised CPU
+// conversion does the same; payload bits are not a parity target).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint16_t f16_from_f32(float f) {
+  const uint32_t u = __float_as_uint(f);
+  if ((u & 0x7FFFFFFFu) > 0x7F800000u)
+    return (uint16_t)(((u >> 16) & 0x8000u) | 0x7E00u | ((u >> 13) & 0x3FFu));
+  return __half_as_ushort(__float2half_rn(f));
+}
+
+__device__ __forceinline__ float f16_to_f32(uint16_t h) {
+  return __half2float(__ushort_as_half(h));
+}
+
+__device__ __forceinline__ uint16_t bf16_from_f32(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+__device__ __forceinline__ float bf16_to_f32(uint16_t h) {
+  return __uint_as_float(((uint32_t)h) << 16);
+}
+
+// E4M3 -> binary16 is exact; the NaN code keeps sign and mantissa (0x7F80).
+__device__ __forceinline__ uint16_t e4m3_to_f16(uint32_t b) {
+  if ((b & 0x7Fu) == 0x7Fu) return (uint16_t)(((b & 0x80u) << 8) | 0x7F80u);
+  return f16_from_f32(e4m3_to_f32(b));
+}
+
+// |v| as fp32 bits: comparing these as unsigned integers orders magnitudes
+// with every NaN above +Inf, which is the NaN-propagating max torch.max uses.
+__device__ __forceinline__ uint32_t mag_bits(float v) {
+  return __float_as_uint(v) & 0x7FFFFFFFu;
+}
+
+__device__ __forceinline__ bool bits_nonfinite(uint32_t mag) { return mag >= 0x7F800000u; }
+
+// Warp-level max of unsigned values.
+__device__ __forceinline__ uint32_t warp_max_u32(uint32_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+
+// Merge a block-reduced magnitude into a module's telemetry pair
+// (gpu_amax: running NaN-propagating max; gpu_has_nonfinite: max with 1).
+// amax holds non-negative floats or NaN, whose bit patterns order correctly
+// as signed integers, so one integer atomicMax implements torch.maximum.
+__device__ __forceinline__ void telem_commit(float* amax, int* flag, uint32_t mag) {
+  if (amax) atomicMax(reinterpret_cast<int*>(amax), (int)mag);
+  if (flag && bits_nonfinite(mag)) atomicMax(flag, 1);
+}
+
+}  // namespace apa

@@ -1,0 +1,6 @@
+// Single translation unit for libapa_kernels.so: the kernels share the
+// device status word (apa::g_status), so they are compiled together rather
+// than as relocatable device code.
+#include "cast.cu"
+#include "gemm.cu"
+#include "ladder.cu"

@@ -1,0 +1,192 @@
+/*
+ * C ABI of libapa_kernels.so: the B200 (sm_100a) kernels behind the APA
+ * per-layer precision path. Plain pointers, sizes and a cudaStream_t passed
+ * as void*; no framework types. Every entry point returns an APA_* status
+ * (0 on success) and never exits or traps. Device pointers are caller-owned
+ * (the Python layer allocates them with torch's caching allocator); the
+ * kernels allocate nothing.
+ *
+ * Shapes are row-major with an explicit leading dimension (elements).
+ * Reference = Adaptive Precision Ascension, apa/ (file:line cited per entry).
+ */
+#ifndef APA_KERNELS_H
+#define APA_KERNELS_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define APA_OK 0
+#define APA_ERR_INVALID 1     /* null pointer, negative/zero size, leading dimension too small */
+#define APA_ERR_ALIGN 2       /* operand not 16-byte aligned where the TMA path needs it */
+#define APA_ERR_UNSUPPORTED 3 /* dtype / rung combination not provided */
+#define APA_ERR_CUDA 4        /* launch failure or missing driver entry point */
+
+/* element types */
+#define APA_DT_F32 0
+#define APA_DT_F16 1
+#define APA_DT_BF16 2
+#define APA_DT_E4M3 3
+
+/* ladder rungs, apa/config.py:5-7 (LEVEL_FP8, LEVEL_FP16, LEVEL_TF32) */
+#define APA_RUNG_FP8 0
+#define APA_RUNG_FP16 1
+#define APA_RUNG_TF32 2
+
+/* GEMM epilogues for apa_gemm_tn */
+#define APA_EPI_FWD 0
+#define APA_EPI_DGRAD 1
+#define APA_EPI_WGRAD 2
+
+/* Library ABI version (bumped on any signature change). */
+int apa_abi_version(void);
+
+/* Human-readable text for a status code. */
+const char* apa_status_string(int status);
+
+/* Read (and optionally clear) the device status word that bounded waits set
+ * when they give up. 0 means no kernel has timed out. Synchronous. */
+int apa_get_device_status(unsigned int* out, int clear);
+
+/*
+ * Cast a [rows, cols] matrix to dst_dtype with fused telemetry.
+ * Replaces: APABoundaryCast.forward x.to(working_dtype) (apa/layers.py:17-21),
+ * APALinear.refresh_working_copy weight_master.to(dtype) (layers.py:368-372),
+ * the E4M3 cast of grad_output in backward (layers.py:225, :243), and the
+ * track_telemetry_on_tensor pass on each of those tensors (telemetry.py:7-21,
+ * called at layers.py:142-143, :211).
+ *   dst / dst_t        nullable: row-major copy and transposed copy [cols, rows]
+ *   amax, flag         nullable: running NaN-propagating max of |value| and
+ *                      max(flag, 1) on any NaN/Inf, over the cast values, or
+ *                      over the source values when telem_on_source != 0
+ *   merge_amax         nullable: a pending amax (e.g. the weight's, taken when
+ *                      the working copy was made) merged into amax/flag
+ *   colsum_partial     nullable: [ceil(rows/64), cols] fp32 partial column
+ *                      sums of the cast values (bias gradient, layers.py:241)
+ * src_dtype: F32, F16 or BF16; dst_dtype: E4M3, F16, F32 (BF16 also accepted).
+ */
+int apa_cast(const void* src, int src_dtype, int64_t rows, int64_t cols, int64_t ld_src,
+             void* dst, int dst_dtype, int64_t ld_dst, void* dst_t, int64_t ld_dst_t,
+             float* amax, int32_t* flag, int telem_on_source, const float* merge_amax,
+             float* colsum_partial, void* stream);
+
+/* amax / nonfinite telemetry of a flat array of n elements of dtype.
+ * Replaces: track_telemetry_on_tensor (apa/telemetry.py:7-21) where no fused
+ * kernel produced the tensor (APALinear.track_telemetry, layers.py:374-389;
+ * the non-APA backward hooks, manager.py:79-84). */
+int apa_amax(const void* src, int dtype, int64_t n, float* amax, int32_t* flag, void* stream);
+
+/* Underflow ratio of a flat array: #(0 < |g| < vmin) / #(|g| > 0) in fp32,
+ * 0 when nothing is nonzero; stored in *ratio_out, or folded into it as a
+ * running max when running_max != 0. counters: 3 zeroed u64 scratch words,
+ * zero again on return.
+ * Replaces: compute_underflow_ratio (apa/telemetry.py:23-39) and
+ * APALinear.update_underflow_metric (apa/layers.py:404-407) when called on a
+ * tensor outside the fused weight-gradient GEMM. */
+int apa_underflow_ratio(const void* src, int dtype, int64_t n, float vmin, unsigned long long* counters,
+                        float* ratio_out, int running_max, void* stream);
+
+/* Fold a stored amax into a telemetry pair (amax max, flag if non-finite). */
+int apa_merge_telemetry(float* amax, int32_t* flag, const float* src_amax, void* stream);
+
+/* Bias gradient from apa_cast's colsum_partial: sum the nparts rows of
+ * partials per column, round to work_dtype (the engine's cast to bias_work's
+ * dtype) and write the fp32 value to out (bias_master.grad), or add it when
+ * accumulate != 0.
+ * Replaces: grad_bias in APALinearFunction.backward (layers.py:239-241,
+ * :265-266, :274-275, :290-291) and its copy in _sync_grads_to_master
+ * (manager.py:200-204). */
+int apa_colsum_finalize(const float* partial, int64_t nparts, int64_t cols, int work_dtype,
+                        float* out, int accumulate, void* stream);
+
+/* Set n int32 device words (given by a device array of pointers) to zero.
+ * Replaces: the per-step flag resets in APAManager.pre_step (manager.py:161-168). */
+int apa_zero_list(int32_t* const* ptrs, int n, void* stream);
+
+/*
+ * Forward GEMM: y[M,N] = xq[M,K] . wq[N,K]^T + bias, fused amax/NaN telemetry
+ * of y into amax/flag.
+ * Replaces: APALinearFunction.forward's per-rung GEMM (layers.py:158-182,
+ * _call_scaled_mm layers.py:23-60) and track_telemetry_on_tensor(result)
+ * (layers.py:186).
+ * rung FP8: xq, wq E4M3, bias E4M3 (nullable), y fp32.
+ * rung FP16: xq, wq, bias fp16, y fp16.  rung TF32: all fp32.
+ * xq and wq rows must be 16-byte aligned (ld * element size % 16 == 0).
+ */
+int apa_linear_fwd(int rung, const void* xq, int64_t ldx, const void* wq, int64_t ldw,
+                   const void* bias_q, void* y, int64_t ldy, int64_t M, int64_t N, int64_t K,
+                   float* amax, int32_t* flag, void* stream);
+
+/*
+ * Input-gradient GEMM: dx[M,K] = cast(cast(dyq[M,N] . wq[N,K], working dtype), dx_dtype).
+ * wqt is the transposed working weight [K, N]. bc_amax / bc_flag (nullable)
+ * receive the telemetry of the working-dtype gradient.
+ * Replaces: grad_input in APALinearFunction.backward (layers.py:233-234,
+ * :247-255, :268-269, :277-278), the autograd engine's cast of it to x_cast's
+ * dtype, ToCopyBackward to x's dtype, and the boundary_cast backward hook's
+ * track_telemetry_on_tensor (manager.py:79-84).
+ */
+int apa_linear_dgrad(int rung, const void* dyq, int64_t lddy, const void* wqt, int64_t ldwt,
+                     void* dx, int dx_dtype, int64_t lddx, int64_t M, int64_t N, int64_t K,
+                     float* bc_amax, int32_t* bc_flag, void* stream);
+
+/*
+ * Weight-gradient GEMM: dw[N,K] = f32(cast(dyq[M,N]^T . xq[M,K], working dtype))
+ * from the transposed operands dyqt[N,M] and xqt[K,M]; accumulate != 0 adds
+ * into dw. Counts the nonzero and below-threshold elements of the unrounded
+ * (FP16: fp16-rounded) gradient in counters[0..1] (counters[2] is a CTA
+ * ticket; all three must be zero on entry and are zero again on return), and
+ * the last CTA folds counters[1]/counters[0] into *ratio_max as a running max.
+ * Thresholds: 2^-6 (FP8), 6.1035e-5 (FP16), 0 (TF32: no counting).
+ * Replaces: grad_weight in APALinearFunction.backward (layers.py:235-238,
+ * :256-264, :270-273, :279-282), compute_underflow_ratio (telemetry.py:23-39)
+ * with its per-layer .item() sync, update_underflow_metric (layers.py:404-407)
+ * and the weight half of _sync_grads_to_master (manager.py:191-199).
+ */
+int apa_linear_wgrad(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt,
+                     float* dw, int64_t lddw, int64_t M, int64_t N, int64_t K, int accumulate,
+                     unsigned long long* counters, float* ratio_max, void* stream);
+
+/*
+ * The same tcgen05 GEMM with a chosen epilogue and no telemetry side effects,
+ * optional N tile (128/256, 0 = automatic) and grid cap (0 = one CTA per SM).
+ * Used to time the bare GEMM against the fused entry points.
+ */
+int apa_gemm_tn(int rung, int epilogue, const void* A, int64_t lda, const void* B, int64_t ldb,
+                void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
+                int tile_n, int grid_cap, void* stream);
+
+/*
+ * Ladder evaluation on device, one launch per step.
+ * Replaces: APAManager._check_hard_overflow (manager.py:178-189),
+ * _do_full_evaluation (manager.py:206-261) and _escalate_module's level/EMA
+ * update (manager.py:267-293); the host then needs one small read of `out`
+ * instead of 3 .item() syncs per module.
+ *
+ * Inputs per APA module i < L (device arrays): amax_ptr[i], ratio_ptr[i],
+ * flag_ptr[i] point at the module's gpu_amax / gpu_underflow_ratio /
+ * gpu_has_nonfinite; level[i] (int32) and ema[i] (double) are the ladder state,
+ * updated in place. Per non-APA leaf j < O: oamax_ptr[j], oflag_ptr[j].
+ * `global` (nullable, int32[1 + 3L + 2O]): when given, the telemetry is read
+ * from this already-reduced vector (see apa_ladder_pack) instead of the
+ * pointers, so every data-parallel rank decides identically.
+ * `out` (int32[4 + 2L + O] + double[2L + O] as described in apa_ladder.cu) receives
+ * the decision record the host uses for logging.
+ */
+int apa_ladder_pack(int L, const float* const* amax_ptr, const float* const* ratio_ptr,
+                    const int32_t* const* flag_ptr, int O, const float* const* oamax_ptr,
+                    const int32_t* const* oflag_ptr, int32_t* packed, void* stream);
+
+int apa_ladder_eval(int L, float* const* amax_ptr, float* const* ratio_ptr, int32_t* const* flag_ptr,
+                    int32_t* level, double* ema, int O, float* const* oamax_ptr, int32_t* const* oflag_ptr,
+                    const int32_t* global, int64_t step_count, int64_t check_interval, double theta,
+                    double alpha, void* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* APA_KERNELS_H */

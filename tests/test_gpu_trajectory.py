@@ -1,0 +1,161 @@
+"""Escalation trajectories through the drop-in API.
+
+cfg0: the quick-start MLP (APALinear(768,768) -> ReLU -> LayerNorm ->
+APALinear(768,10), AdamW 1e-3, research_default, one seeded batch of 64,
+200 steps, 49 elements x1e3 at steps 50 and 150). The event sequence
+(step, module, reason, old level, new level) and the skipped steps must equal
+the reference's (tests/golden/cfg0_trajectory.json, produced by running the
+reference on CPU); trigger values must agree (NaN with NaN).
+
+cfg1 variants at the full 8192x4096x4096 shape: the outlier variant must skip
+and escalate FP8->FP16 on the first step; the underflow variant must escalate
+through SILENT_UNDERFLOW on the step the oracle's EMA recursion predicts from
+the kernel's own (bit-exact) underflow ratio.
+"""
+import json
+import math
+import os
+
+import pytest
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+G = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def _capture(mgr):
+    events = []
+
+    def cap(d):
+        d = dict(d)
+        d.pop("timestamp", None)
+        events.append(d)
+    mgr.logger._log_event = cap
+    return events
+
+
+def test_cfg0_trajectory_matches_reference():
+    from apa import APAConfig, APALinear, APAManager
+    with open(os.path.join(G, "cfg0_trajectory.json")) as fh:
+        gold = json.load(fh)
+    torch.manual_seed(0)
+    cfg = APAConfig.research_default(device="cuda")
+
+    class MLP(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.fc1 = APALinear(768, 768, config=cfg)
+            self.relu = nn.ReLU()
+            self.norm = nn.LayerNorm(768)
+            self.fc2 = APALinear(768, 10, config=cfg)
+
+        def forward(self, x):
+            return self.fc2(self.norm(self.relu(self.fc1(x))))
+
+    m = MLP().cuda()
+    for k, v in m.state_dict().items():
+        if k in gold["w0_checksum"]:
+            assert float(v.double().sum()) == pytest.approx(gold["w0_checksum"][k], rel=1e-6, abs=1e-6), k
+    mgr = APAManager(m, cfg)
+    events = _capture(mgr)
+    opt = torch.optim.AdamW(mgr.get_trainable_parameters(), lr=1e-3)
+    g = torch.Generator().manual_seed(0)
+    x0 = torch.randn(64, 768, generator=g).cuda()
+    y0 = torch.randint(0, 10, (64,), generator=g).cuda()
+    spikes = {int(k): torch.tensor(v) for k, v in gold["spike_idx"].items()}
+    skips = []
+    for step in range(200):
+        x = x0.clone()
+        if step in spikes:
+            x.view(-1)[spikes[step].cuda()] *= 1e3
+        mgr.pre_step()
+        opt.zero_grad(set_to_none=True)
+        loss = F.cross_entropy(m(x), y0)
+        loss.backward()
+        if mgr.post_backward_sync_and_eval():
+            opt.step()
+        else:
+            opt.zero_grad(set_to_none=True)
+            skips.append(step)
+    assert skips == gold["skips"]
+    key = lambda e: (e["event"], e["step"], e.get("module"), e.get("reason"), e.get("old_level"),
+                     e.get("new_level"), tuple(e.get("trigger_modules", ())))
+    assert [key(e) for e in events] == [key(e) for e in gold["events"]]
+    for a, b in zip(events, gold["events"]):
+        if "trigger_value" in b:
+            tb = b["trigger_value"]
+            if isinstance(tb, float) and math.isnan(tb):
+                assert math.isnan(a["trigger_value"])
+            else:
+                assert a["trigger_value"] == pytest.approx(tb, rel=1e-2)
+    assert [m.fc1.level, m.fc2.level] == gold["levels"][-1]
+
+
+def _cfg1_layer(cfg):
+    from apa import APALinear
+    torch.manual_seed(0)
+    return APALinear(4096, 4096, config=cfg)
+
+
+def test_cfg1_outlier_variant_escalates():
+    from apa import APAConfig, APAManager
+    cfg = APAConfig(device="cuda", check_interval=1)
+    lin = _cfg1_layer(cfg)
+    mgr = APAManager(nn.Sequential(lin), cfg)
+    events = _capture(mgr)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(8192, 4096, device="cuda", generator=g).to(torch.bfloat16)
+    n_out = int(x.numel() * 0.0005)
+    idx = torch.randperm(x.numel(), device="cuda", generator=g)[:n_out]
+    x.view(-1)[idx] *= 500
+    x.requires_grad_(True)
+    dy = torch.randn(8192, 4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1))
+    mgr.pre_step()
+    lin(x).backward(dy)
+    ok = mgr.post_backward_sync_and_eval()
+    assert not ok
+    assert lin.level == 1
+    esc = [e for e in events if e["event"] == "escalation" and e["module"] == "0"]
+    assert esc and esc[0]["reason"] == "OVERFLOW" and math.isnan(esc[0]["trigger_value"])
+
+
+def test_cfg1_underflow_variant_escalates_on_predicted_step():
+    from apa import APAConfig, APAManager
+    cfg = APAConfig(device="cuda", check_interval=1)
+    lin = _cfg1_layer(cfg)
+    mgr = APAManager(nn.Sequential(lin), cfg)
+    events = _capture(mgr)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(8192, 4096, device="cuda", generator=g)
+    mask = torch.rand(8192, 4096, device="cuda", generator=g) < 0.5
+    x = torch.where(mask, x * 1e-4, x).to(torch.bfloat16)
+    dy = torch.randn(8192, 4096, device="cuda", generator=torch.Generator(device="cuda").manual_seed(1)) * 5e-4
+    ratio = None
+    ema = 0.0
+    predicted = None
+    for step in range(1, 80):
+        mgr.pre_step()
+        lin(x).backward(dy)
+        if ratio is None:
+            ratio = lin.gpu_underflow_ratio.item()
+            assert 0.40 < ratio < 0.45, ratio
+            # the reference's recursion (manager.py:232-235) on this ratio
+            e, n = 0.0, 0
+            while True:
+                n += 1
+                e = cfg.ema_alpha * e + (1 - cfg.ema_alpha) * ratio
+                if e > cfg.theta_underflow:
+                    predicted = n
+                    break
+        assert lin.gpu_underflow_ratio.item() == ratio   # the same input gives the same exact counts
+        assert mgr.post_backward_sync_and_eval()
+        if lin.level == 1:
+            assert step == predicted
+            break
+    else:
+        pytest.fail("no SILENT_UNDERFLOW escalation")
+    esc = [e for e in events if e["event"] == "escalation"]
+    assert esc[0]["reason"] == "SILENT_UNDERFLOW" and esc[0]["step"] == predicted

@@ -1,0 +1,67 @@
+"""Host-side behaviour that needs no GPU: config presets and defaults,
+forensic file derivation, constants, module construction and discovery."""
+import math
+
+import pytest
+import torch
+import torch.nn as nn
+
+
+def test_constants_match_reference():
+    from apa import config as C
+    assert (C.LEVEL_FP8, C.LEVEL_FP16, C.LEVEL_TF32) == (0, 1, 2)
+    assert C.THRESHOLDS_MAX[0] == 0.90 * 448.0 and C.THRESHOLDS_MAX[1] == 0.90 * 65504.0
+    assert math.isinf(C.THRESHOLDS_MAX[2])
+    assert C.THRESHOLDS_MIN == {0: 0.015625, 1: 6.1035e-5, 2: 0.0}
+    assert C.DTYPE_MAP[0] == torch.float8_e4m3fn and C.DTYPE_MAP[1] == torch.float16
+
+
+def test_presets_and_defaults():
+    from apa import APAConfig
+    d = APAConfig()
+    assert (d.gamma, d.theta_underflow, d.ema_alpha, d.check_interval, d.device) == (0.9, 0.4, 0.95, 1, "cuda")
+    c = APAConfig.conservative()
+    assert (c.gamma, c.theta_underflow, c.check_interval) == (0.8, 0.3, 1)
+    a = APAConfig.aggressive(check_interval=3)
+    assert (a.gamma, a.theta_underflow, a.check_interval) == (0.95, 0.5, 3)
+    r = APAConfig.research_default()
+    assert (r.gamma, r.theta_underflow, r.check_interval) == (0.9, 0.4, 4)
+
+
+@pytest.mark.parametrize("log,expect", [("a/b/log.jsonl", "a/b/log_forensic.jsonl"),
+                                        ("noext", "noext_forensic.jsonl"),
+                                        ("x.y.z", "x.y_forensic.jsonl"),
+                                        (None, "apa_forensic.jsonl")])
+def test_forensic_file_derivation(log, expect):
+    from apa import APAConfig
+    c = APAConfig(log_file=log, enable_forensic_logging=True)
+    assert c.forensic_log_file == expect
+    assert APAConfig(log_file=log).forensic_log_file is None
+
+
+def test_module_discovery_and_state_dict_on_cpu_construction():
+    """Construction needs no GPU; the same seed gives the same weights as
+    nn.Linear's initialisation rule on the CPU generator."""
+    from apa import APAConfig, APALinear, APAManager
+    cfg = APAConfig(device="cpu")
+    torch.manual_seed(3)
+    lin = APALinear(32, 8, config=cfg)
+    torch.manual_seed(3)
+    ref = nn.Linear(32, 8)
+    assert torch.equal(lin.weight_master, ref.weight) and torch.equal(lin.bias_master, ref.bias)
+    model = nn.Sequential(nn.Embedding(10, 32), lin, nn.LayerNorm(8))
+    mgr = APAManager(model, cfg)
+    assert list(mgr.apa_modules) == ["1"]
+    assert list(mgr.other_modules) == ["0", "1.boundary_cast", "2"]
+    assert len(mgr.get_trainable_parameters()) == 5
+    assert set(lin.state_dict()) == {"weight_master", "bias_master", "gpu_amax", "gpu_underflow_ratio",
+                                     "gpu_has_nonfinite"}
+
+
+def test_no_cpu_compute_path():
+    """The product refuses to compute on CPU tensors instead of falling back."""
+    from apa import APAConfig, APALinear
+    from apa._lib import APAKernelError
+    lin = APALinear(16, 16, config=APAConfig(device="cpu"))
+    with pytest.raises(APAKernelError):
+        lin(torch.randn(2, 16))
