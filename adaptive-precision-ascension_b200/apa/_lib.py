@@ -16,7 +16,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libapa_kernels.so")
 
 OK, ERR_INVALID, ERR_ALIGN, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3, 4
-DT_F32, DT_F16, DT_BF16, DT_E4M3 = 0, 1, 2, 3
+DT_F32, DT_F16, DT_BF16, DT_E4M3, DT_TF32 = 0, 1, 2, 3, 4
 RUNG_FP8, RUNG_FP16, RUNG_TF32 = 0, 1, 2
 EPI_FWD, EPI_DGRAD, EPI_WGRAD = 0, 1, 2
 
@@ -71,7 +71,14 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+# number of kernel-library calls made (each entry point launches one kernel);
+# bench.py reads it to report how many of this library's kernels it timed
+calls = 0
+
+
 def check(status: int, what: str) -> None:
+    global calls
+    calls += 1
     if status != OK:
         msg = lib().apa_status_string(status).decode()
         raise APAKernelError(f"{what} failed: status {status} ({msg})")

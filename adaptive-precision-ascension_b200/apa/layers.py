@@ -63,6 +63,12 @@ def _working(level: int) -> torch.dtype:
     return DTYPE_MAP[level] if DTYPE_MAP[level] is not None else torch.float32
 
 
+def _operand_code(level: int) -> int:
+    """C-ABI dtype code of the GEMM operands at a level: the working dtype,
+    except that TF32-rung operands are stored rounded to the TF32 grid."""
+    return _lib.DT_TF32 if level == LEVEL_TF32 else _lib.dt_code(_working(level))
+
+
 def _alloc_2d(rows: int, cols: int, dtype: torch.dtype, device) -> torch.Tensor:
     """[rows, cols] view of a buffer whose row pitch is padded to 16 bytes."""
     buf = torch.empty(rows, _pad(cols, _elem_size(dtype)), dtype=dtype, device=device)
@@ -161,13 +167,14 @@ class _APALinearFn(torch.autograd.Function):
 
         # boundary cast (+ transposed copy for wgrad) with telemetry of x_cast
         # and the weight's pending amax (layers.py:17-21, :142-143)
-        if x.dtype == wd and _tma_ok(x2):
+        opc = _operand_code(level)
+        if x.dtype == wd and level != LEVEL_TF32 and _tma_ok(x2):
             xq, new_xq = x2, False
         else:
             xq, new_xq = _alloc_2d(M, K, wd, dev), True
         xqt = _alloc_2d(K, M, wd, dev) if need_dw else None
         st = lib.apa_cast(x2.data_ptr(), _lib.dt_code(x.dtype), M, K, x2.stride(0),
-                          xq.data_ptr() if new_xq else None, _lib.dt_code(wd), xq.stride(0),
+                          xq.data_ptr() if new_xq else None, opc, xq.stride(0),
                           _lib.ptr(xqt), xqt.stride(0) if xqt is not None else 0,
                           mod.gpu_amax.data_ptr(), mod.gpu_has_nonfinite.data_ptr(), 0,
                           mod._w_pending.data_ptr(), None, s)
@@ -214,7 +221,7 @@ class _APALinearFn(torch.autograd.Function):
 
         # grad_output telemetry (layers.py:211), its working-dtype copy, the
         # transposed copy for wgrad and the bias partial sums, in one pass
-        if dy2.dtype == wd and _tma_ok(dy2):
+        if dy2.dtype == wd and level != LEVEL_TF32 and _tma_ok(dy2):
             dyq, new_dyq = dy2, False
         else:
             dyq, new_dyq = _alloc_2d(M, N, wd, dev), True
@@ -222,7 +229,7 @@ class _APALinearFn(torch.autograd.Function):
         nparts = (M + 63) // 64
         partial = torch.empty(nparts, N, dtype=torch.float32, device=dev) if need_db else None
         st = lib.apa_cast(dy2.data_ptr(), _lib.dt_code(dy2.dtype), M, N, dy2.stride(0),
-                          dyq.data_ptr() if (new_dyq and need_dx) else None, _lib.dt_code(wd), dyq.stride(0),
+                          dyq.data_ptr() if (new_dyq and need_dx) else None, _operand_code(level), dyq.stride(0),
                           _lib.ptr(dyqt), dyqt.stride(0) if dyqt is not None else 0,
                           mod.gpu_amax.data_ptr(), mod.gpu_has_nonfinite.data_ptr(), 1, None,
                           _lib.ptr(partial), s)
@@ -243,7 +250,7 @@ class _APALinearFn(torch.autograd.Function):
             dx = torch.empty(M, K, dtype=ctx.xdtype, device=dev)
             bc = mod.boundary_cast
             st = lib.apa_linear_dgrad(level, dyq.data_ptr(), dyq.stride(0), wqt.data_ptr(), wqt.stride(0),
-                                      dx.data_ptr(), _lib.dt_code(ctx.xdtype), K, M, K, N,
+                                      dx.data_ptr(), _lib.dt_code(ctx.xdtype), K, M, N, K,
                                       _lib.ptr(getattr(bc, "gpu_amax", None)),
                                       _lib.ptr(getattr(bc, "gpu_has_nonfinite", None)), s)
             _lib.check(st, "apa_linear_dgrad")
@@ -287,6 +294,15 @@ class _APALinearFn(torch.autograd.Function):
         return dx, None, None, None
 
 
+def _drop_working_copy_keys(state_dict, prefix, *args):
+    """The reference registers the working copies as parameters while a layer
+    is at TF32 (its ``.to(float32)`` returns the master Parameter itself), so
+    its checkpoints can carry ``weight_work`` / ``bias_work`` aliases of the
+    masters. They are not state here; drop them so such checkpoints load."""
+    for k in ("weight_work", "bias_work"):
+        state_dict.pop(prefix + k, None)
+
+
 class APALinear(nn.Module):
     def __init__(self, in_features: int, out_features: int, bias: bool = True, config: APAConfig = APAConfig()):
         super().__init__()
@@ -327,6 +343,7 @@ class APALinear(nn.Module):
         self._epoch = 0
         self._grad_epoch = -1
         self._grad_ready_cb = None
+        self._register_load_state_dict_pre_hook(_drop_working_copy_keys)
         self.reset_parameters()
         if dev.type != "cpu":
             with torch.no_grad():
@@ -372,14 +389,13 @@ class APALinear(nn.Module):
         self._epoch += 1
         with torch.no_grad():
             if level == LEVEL_TF32:
-                self.weight_work = W
-                if _tma_ok(W.data):
-                    self._wq = W.data
-                    new_wq = False
-                else:
-                    if self._wq_level != level or self._wq is None or self._wq.data_ptr() == W.data_ptr():
-                        self._wq = _alloc_2d(N, K, wd, W.device)
-                    new_wq = True
+                # the working weight is the master itself (stored as a plain
+                # attribute so it is not registered twice as a parameter); the
+                # GEMM reads a TF32-rounded copy
+                self.__dict__["weight_work"] = W
+                if self._wq_level != level or self._wq is None or self._wq.dtype != wd:
+                    self._wq = _alloc_2d(N, K, wd, W.device)
+                new_wq = True
             else:
                 if self._wq_level != level or self._wq is None or self._wq.dtype != wd:
                     self._wq = _alloc_2d(N, K, wd, W.device)
@@ -389,7 +405,7 @@ class APALinear(nn.Module):
                 self._wqt = _alloc_2d(K, N, wd, W.device)
             want_t = self._needs_wt
             st = lib.apa_cast(W.data_ptr(), _lib.DT_F32, N, K, W.stride(0),
-                              self._wq.data_ptr() if new_wq else None, _lib.dt_code(wd), self._wq.stride(0),
+                              self._wq.data_ptr() if new_wq else None, _operand_code(level), self._wq.stride(0),
                               self._wqt.data_ptr() if want_t else None, self._wqt.stride(0),
                               self._w_pending.data_ptr(), None, 0, None, None, s)
             _lib.check(st, "apa_cast(weight)")
@@ -398,7 +414,7 @@ class APALinear(nn.Module):
                 b = self.bias_master
                 if level == LEVEL_TF32:
                     self._bq = b.data
-                    self.bias_work = b
+                    self.__dict__["bias_work"] = b
                 else:
                     if self._bq is None or self._bq.dtype != wd or self._wq_level != level:
                         self._bq = torch.empty(N, dtype=wd, device=b.device)
@@ -415,7 +431,7 @@ class APALinear(nn.Module):
         N, K = W.shape
         if self._wqt is None or self._wqt.dtype != wd:
             self._wqt = _alloc_2d(K, N, wd, W.device)
-        st = _lib.lib().apa_cast(W.data_ptr(), _lib.DT_F32, N, K, W.stride(0), None, _lib.dt_code(wd), 0,
+        st = _lib.lib().apa_cast(W.data_ptr(), _lib.DT_F32, N, K, W.stride(0), None, _operand_code(self.level), 0,
                                  self._wqt.data_ptr(), self._wqt.stride(0), None, None, 0, None, None,
                                  _lib.stream_handle(W.device))
         _lib.check(st, "apa_cast(weight^T)")

@@ -83,7 +83,11 @@ __device__ __forceinline__ uint16_t f16_from_f32(float f) {
   return __half_as_ushort(__float2half_rn(f));
 }
 
+// binary16 -> fp32 is exact; a NaN keeps its sign and payload (the hardware
+// conversion would return a canonical, sign-less NaN).
 __device__ __forceinline__ float f16_to_f32(uint16_t h) {
+  if ((h & 0x7C00u) == 0x7C00u && (h & 0x3FFu))
+    return __uint_as_float(((uint32_t)(h & 0x8000u) << 16) | 0x7FC00000u | ((uint32_t)(h & 0x3FFu) << 13));
   return __half2float(__ushort_as_half(h));
 }
 
@@ -93,6 +97,15 @@ __device__ __forceinline__ uint16_t bf16_from_f32(float f) {
 
 __device__ __forceinline__ float bf16_to_f32(uint16_t h) {
   return __uint_as_float(((uint32_t)h) << 16);
+}
+
+// fp32 -> the TF32 operand grid (10 mantissa bits), round half to even,
+// kept in fp32 storage. The tensor core reads only the top 19 bits of an fp32
+// operand; rounding first halves the product error compared to dropping the
+// low bits. Inf/NaN pass through.
+__device__ __forceinline__ uint32_t tf32_rn_bits(uint32_t u) {
+  if ((u & 0x7F800000u) == 0x7F800000u) return u;
+  return (u + 0xFFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
 }
 
 // E4M3 -> binary16 is exact; the NaN code keeps sign and mantissa (0x7F80).

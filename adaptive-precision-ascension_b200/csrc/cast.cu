@@ -126,6 +126,7 @@ struct CastParams {
   float* colsum;          // [ceil(rows/64), cols] partial sums of the cast values
   int telem_on_source;
   int vec_src, vec_dst, vec_dst_t;
+  int tf32;               // DST fp32 only: stored operands rounded to TF32
 };
 
 template <int SRC, int DST>
@@ -193,12 +194,18 @@ __global__ void __launch_bounds__(kThreads) cast_kernel(CastParams p) {
       if (in) mag = max(mag, p.telem_on_source ? mag_bits(v[j]) : code_mag_bits<DST>(code[j]));
     }
     if (p.dst) {
+      uint32_t out[kSeg];
+#pragma unroll
+      for (int j = 0; j < kSeg; ++j) {
+        if constexpr (DST == APA_DT_F32) out[j] = p.tf32 ? tf32_rn_bits(code[j]) : code[j];
+        else out[j] = code[j];
+      }
       if (full) {
-        store16<DST>(p.dst, row * p.ld_dst + col0, code, p.vec_dst != 0);
+        store16<DST>(p.dst, row * p.ld_dst + col0, out, p.vec_dst != 0);
       } else if (row_ok) {
 #pragma unroll
         for (int j = 0; j < kSeg; ++j)
-          if (col0 + j < p.cols) store_code<DST>(p.dst, row * p.ld_dst + col0 + j, code[j]);
+          if (col0 + j < p.cols) store_code<DST>(p.dst, row * p.ld_dst + col0 + j, out[j]);
       }
     }
     if (stage) {
@@ -219,6 +226,7 @@ __global__ void __launch_bounds__(kThreads) cast_kernel(CastParams p) {
       for (int i = 0; i < kSeg; ++i) {
         tcode[i] = tile[rs + i][jc];
         csum += decode<DST>(tcode[i]);
+        if constexpr (DST == APA_DT_F32) tcode[i] = p.tf32 ? tf32_rn_bits(tcode[i]) : tcode[i];
       }
       if (p.dst_t && tcol < p.cols) {
         if (trow0 + kSeg <= p.rows) {
@@ -402,6 +410,8 @@ extern "C" int apa_cast(const void* src, int src_dtype, int64_t rows, int64_t co
   if (!src || rows < 0 || cols < 0 || ld_src < cols) return APA_ERR_INVALID;
   if (dst && ld_dst < cols) return APA_ERR_INVALID;
   if (dst_t && ld_dst_t < rows) return APA_ERR_INVALID;
+  const int tf32 = dst_dtype == APA_DT_TF32;
+  if (tf32) dst_dtype = APA_DT_F32;
   const int es_src = esize(src_dtype), es_dst = esize(dst_dtype);
   if (!es_src || !es_dst || src_dtype == APA_DT_E4M3) return APA_ERR_UNSUPPORTED;
   if (rows == 0 || cols == 0) {
@@ -412,7 +422,7 @@ extern "C" int apa_cast(const void* src, int src_dtype, int64_t rows, int64_t co
   p.src = src; p.rows = rows; p.cols = cols; p.ld_src = ld_src;
   p.dst = dst; p.ld_dst = ld_dst; p.dst_t = dst_t; p.ld_dst_t = ld_dst_t;
   p.amax = amax; p.flag = reinterpret_cast<int*>(flag); p.merge_amax = merge_amax;
-  p.colsum = colsum_partial; p.telem_on_source = telem_on_source;
+  p.colsum = colsum_partial; p.telem_on_source = telem_on_source; p.tf32 = tf32;
   p.vec_src = aligned16(src, ld_src, es_src);
   p.vec_dst = aligned16(dst, ld_dst, es_dst);
   p.vec_dst_t = aligned16(dst_t, ld_dst_t, es_dst);

@@ -1,0 +1,405 @@
+"""Benchmark: APALinear forward+backward TFLOP/s per ladder rung.
+
+Workload (default): one APALinear at M=8192 tokens, K=4096, N=4096 with fp32
+master weights (Kaiming-uniform, seed 0), bf16 activations ~ N(0,1) (seed 0)
+and upstream gradients ~ N(0,1) (seed 1; fp32 at the FP8/TF32 rungs, fp16 at
+the FP16 rung, the output dtype). A step is the reference's full training
+step for that layer through the public API: APAManager.pre_step (working
+copy), forward, backward, post_backward_sync_and_eval (ladder + the one host
+read); 6*M*N*K FLOPs per step. The headline `value` is the FP8 rung.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With N > 1 (launched by torchrun, one rank per GPU, NCCL) every rank runs the
+same layer on its own 8192-token shard (weak scaling) and the step includes the
+data-parallel gradient all-reduce and the telemetry all-reduce; `value` is the
+whole-job FLOP rate with time taken as the max over ranks.
+
+`--impl reference` times the reference's own implementation of the path (its
+fp8_simulation_mode CPU path, installed under baseline/_ref) on this host's
+cores, FP8 rung, on a bounded number of steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "adaptive-precision-ascension_b200")
+
+M, K, N = 8192, 4096, 4096
+FLOPS_STEP = 6.0 * M * N * K
+METRIC = "APALinear fwd+bwd TFLOP/s (FP8 rung)"
+CONFIG = {"workload": "APALinear 8192x4096x4096 fwd+bwd, full APA step (pre_step, fwd, bwd, ladder)",
+          "M": M, "K": K, "N": N, "x": "bf16 N(0,1) seed 0", "dy": "N(0,1) seed 1, output dtype",
+          "l2": "inputs larger than L2: ~0.8 GB touched per step vs 126 MB L2"}
+
+
+def peaks():
+    p = {"source": "fallback", "hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            d = json.load(fh)
+        p = {"source": "measured", "hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"]}
+    # dense FP8 runs at twice the dense bf16 rate on B200; TF32 at half
+    p["fp8_tflops"] = 2.0 * p["bf16_tflops"]
+    p["fp16_tflops"] = p["bf16_tflops"]
+    p["tf32_tflops"] = 0.5 * p["bf16_tflops"]
+    return p
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (SM clock and throttle reasons)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        self.rows = []
+        if self.proc is None:
+            return
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 8:
+                self.rows.append(parts)
+
+    def summary(self):
+        if not getattr(self, "rows", None):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[4 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def dist_info():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ---------------------------------------------------------------------------
+# our implementation
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    sys.path.insert(0, PKG)
+    import torch
+    import torch.distributed as dist
+    import torch.nn as nn
+    from apa import APAConfig, APALinear, APAManager, _lib
+
+    world, rank, local = dist_info()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    g = torch.Generator(device=dev).manual_seed(0 + 1000 * rank)
+    x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+    g1 = torch.Generator(device=dev).manual_seed(1 + 1000 * rank)
+    dy32 = torch.randn(M, N, device=dev, generator=g1)
+    dy16 = dy32.half()
+
+    def make(level):
+        cfg = APAConfig(device=str(dev), check_interval=1)
+        torch.manual_seed(0)
+        lin = APALinear(K, N, config=cfg)
+        lin.level = level
+        mgr = APAManager(nn.Sequential(lin), cfg)
+        return lin, mgr
+
+    results = {}
+    gemm_roof = None
+    launches = 0
+    clocks = None
+    pk = peaks()
+    for level, name in ((0, "fp8"), (1, "fp16"), (2, "tf32")):
+        lin, mgr = make(level)
+        dy = dy16 if level == 1 else dy32
+        xr = x.detach().requires_grad_(True)
+
+        def step():
+            mgr.pre_step()
+            y = lin(xr)
+            y.backward(dy)
+            xr.grad = None
+            return mgr.post_backward_sync_and_eval()
+
+        for _ in range(args.warmup):
+            step()
+        barrier()
+        c0 = _lib.calls
+        s = torch.cuda.current_stream(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        sampler = ClockSampler(local) if (level == 0 and rank == 0) else None
+        if sampler:
+            sampler.__enter__()
+        e0.record(s)
+        for _ in range(args.steps):
+            step()
+        e1.record(s)
+        barrier()
+        if sampler:
+            sampler.__exit__()
+            clocks = sampler.summary()
+        ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+        if level == 0:
+            launches = (_lib.calls - c0)
+        results[name] = {"ms_per_step": ms, "tflops": world * FLOPS_STEP / ms / 1e9,
+                         "frac_of_peak": FLOPS_STEP / ms / 1e9 / pk[f"{name}_tflops"]}
+        if level == 0:
+            gemm_roof = time_gemm(torch, _lib, lin, xr, dev, pk)
+        del lin, mgr
+        torch.cuda.empty_cache()
+
+    # end to end: host-resident inputs, copied in every step, result read back
+    e2e = run_e2e(torch, make, x, dy32, dev, args, world, barrier, max_over_ranks)
+    out = None
+    if rank == 0:
+        fp8 = results["fp8"]
+        out = {
+            "metric": METRIC, "value": round(fp8["tflops"], 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(fp8["ms_per_step"], 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3",
+            "data": "synthetic", "config": dict(CONFIG, parallelism=f"dp{world}"),
+            "rungs": {k: {"tflops": round(v["tflops"], 2), "ms_per_step": round(v["ms_per_step"], 4),
+                          "frac_of_peak": round(v["frac_of_peak"], 4)} for k, v in results.items()},
+            "roofline": gemm_roof,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "peaks": pk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            out["cpu_baseline"] = cpu_baseline(args, sample_steps=1)
+    if world > 1:
+        dist.destroy_process_group()
+    return out
+
+
+def time_gemm(torch, _lib, lin, xr, dev, pk):
+    """The dominant kernel: the FP8 tcgen05 GEMM (forward, 8192x4096x4096),
+    timed alone with CUDA events on its launching stream."""
+    lib = _lib.lib()
+    wq = lin._wq
+    xq = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=dev)
+    _lib.check(lib.apa_cast(xr.data_ptr(), _lib.DT_BF16, M, K, K, xq.data_ptr(), _lib.DT_E4M3, K, None, 0,
+                            None, None, 0, None, None, _lib.stream_handle(dev)), "cast")
+    y = torch.empty(M, N, device=dev)
+    amax = torch.zeros(1, device=dev)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    s = torch.cuda.current_stream(dev)
+    st = _lib.stream_handle(dev)
+
+    def launch():
+        _lib.check(lib.apa_linear_fwd(0, xq.data_ptr(), K, wq.data_ptr(), wq.stride(0), lin._bq.data_ptr(),
+                                      y.data_ptr(), N, M, N, K, amax.data_ptr(), flag.data_ptr(), st), "fwd")
+
+    for _ in range(5):
+        launch()
+    reps = 50
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(reps):
+        launch()
+    e1.record(s)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / reps * 1e3
+    achieved = 2.0 * M * N * K / (us * 1e-6) / 1e12
+    return {"kernel": "gemm_kernel<E4M3,256,FWD> 8192x4096x4096", "bound": "tensor",
+            "achieved": round(achieved, 1), "peak": pk["fp8_tflops"], "unit": "TFLOP/s",
+            "frac": round(achieved / pk["fp8_tflops"], 4), "us_per_launch": round(us, 2),
+            "peak_note": f"2 x {pk['source']} bf16 cuBLAS burst ({pk['bf16_tflops']} TFLOP/s); "
+                         "spec dense FP8 4500 TFLOP/s",
+            "traffic": None}
+
+
+def run_e2e(torch, make, x, dy32, dev, args, world, barrier, max_over_ranks):
+    lin, mgr = make(0)
+    xh = x.cpu().pin_memory()
+    dyh = dy32.cpu().pin_memory()
+    xd = torch.empty_like(x)
+    dyd = torch.empty_like(dy32)
+    flag_h = torch.zeros(1, dtype=torch.int32).pin_memory()
+
+    def step():
+        xd.copy_(xh, non_blocking=True)
+        dyd.copy_(dyh, non_blocking=True)
+        xr = xd.requires_grad_(True)
+        mgr.pre_step()
+        lin(xr).backward(dyd)
+        ok = mgr.post_backward_sync_and_eval()    # reads the step's decision record back
+        xr.grad = None
+        xr.requires_grad_(False)
+        return ok
+
+    for _ in range(max(2, args.warmup)):
+        step()
+    barrier()
+    s = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    steps = max(3, args.steps // 2)
+    for _ in range(steps):
+        step()
+    e1.record(s)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    rec_bytes = mgr._ladder.nbytes
+    return {"value": round(world * FLOPS_STEP / ms / 1e9, 2), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+            "h2d_bytes_per_step": int(x.numel() * x.element_size() + dy32.numel() * 4),
+            "d2h_bytes_per_step": int(rec_bytes),
+            "api": "APAManager.pre_step / APALinear fwd+bwd / post_backward_sync_and_eval, pinned host inputs"}
+
+
+# ---------------------------------------------------------------------------
+# the reference's CPU path
+# ---------------------------------------------------------------------------
+def _import_reference():
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "apa")):
+        return None, "reference not installed under baseline/_ref"
+    for k in [k for k in sys.modules if k == "apa" or k.startswith("apa.")]:
+        del sys.modules[k]
+    sys.path.insert(0, ref)
+    try:
+        import apa as ref_apa
+    finally:
+        sys.path.remove(ref)
+    if not os.path.abspath(ref_apa.__file__).startswith(os.path.abspath(ref)):
+        return None, "could not import the reference package"
+    return ref_apa, None
+
+
+def ref_step_fn(ref_apa, torch, M_=M):
+    import torch.nn as nn
+    cfg = ref_apa.APAConfig(fp8_simulation_mode=True, device="cpu", check_interval=1)
+    torch.manual_seed(0)
+    lin = ref_apa.APALinear(K, N, config=cfg)
+    mgr = ref_apa.APAManager(nn.Sequential(lin), cfg)
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(M_, K, generator=g).to(torch.bfloat16).requires_grad_(True)
+    dy = torch.randn(M_, N, generator=torch.Generator().manual_seed(1))
+
+    def step():
+        mgr.pre_step()
+        lin(x).backward(dy)
+        x.grad = None
+        return mgr.post_backward_sync_and_eval()
+    return step
+
+
+def cpu_baseline(args, sample_steps=1):
+    import torch
+    ref_apa, why = _import_reference()
+    if ref_apa is None:
+        return {"value": None, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "reference",
+                "sample": why}
+    torch.set_num_threads(os.cpu_count())
+    import contextlib
+    import io
+    step = ref_step_fn(ref_apa, torch)
+    with contextlib.redirect_stdout(io.StringIO()):
+        step()
+        t0 = time.perf_counter()
+        for _ in range(sample_steps):
+            step()
+        dt = (time.perf_counter() - t0) / sample_steps
+    return {"value": round(FLOPS_STEP / dt / 1e12, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "reference",
+            "sample": f"reference fp8_simulation_mode CPU path, FP8 rung, full 8192x4096x4096 step, "
+                      f"{sample_steps} timed step(s) after 1 warm-up, {dt:.2f} s/step, torch {torch.__version__}"}
+
+
+def run_reference(args):
+    world, rank, _ = dist_info()
+    if rank != 0:
+        return None
+    import contextlib
+    import io
+    import torch
+    ref_apa, why = _import_reference()
+    if ref_apa is None:
+        return {"impl": "reference", "unavailable": why}
+    torch.set_num_threads(os.cpu_count())
+    step = ref_step_fn(ref_apa, torch)
+    steps = max(1, min(args.steps, 5))
+    warm = max(1, min(args.warmup, 1))
+    with contextlib.redirect_stdout(io.StringIO()):
+        for _ in range(warm):
+            step()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            step()
+        dt = (time.perf_counter() - t0) / steps
+    v = round(FLOPS_STEP / dt / 1e12, 4)
+    return {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": steps, "warmup": warm, "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
+            "config": dict(CONFIG, parallelism="cpu"),
+            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "reference",
+                             "sample": f"reference fp8_simulation_mode CPU path, FP8 rung, {steps} full steps "
+                                       f"(of the requested {args.steps}) after {warm} warm-up"},
+            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    out = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

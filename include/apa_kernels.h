@@ -30,6 +30,8 @@ extern "C" {
 #define APA_DT_F16 1
 #define APA_DT_BF16 2
 #define APA_DT_E4M3 3
+#define APA_DT_TF32 4 /* apa_cast destination only: fp32 storage rounded to the TF32
+                         grid (round half to even), the operand form of the TF32 rung */
 
 /* ladder rungs, apa/config.py:5-7 (LEVEL_FP8, LEVEL_FP16, LEVEL_TF32) */
 #define APA_RUNG_FP8 0
@@ -66,7 +68,10 @@ int apa_get_device_status(unsigned int* out, int clear);
  *                      the working copy was made) merged into amax/flag
  *   colsum_partial     nullable: [ceil(rows/64), cols] fp32 partial column
  *                      sums of the cast values (bias gradient, layers.py:241)
- * src_dtype: F32, F16 or BF16; dst_dtype: E4M3, F16, F32 (BF16 also accepted).
+ * src_dtype: F32, F16 or BF16; dst_dtype: E4M3, F16, F32, TF32 (BF16 also
+ * accepted). With TF32 the stored values are rounded to the TF32 grid while
+ * telemetry and column sums use the unrounded fp32 values (the reference's
+ * TF32 rung computes in true fp32).
  */
 int apa_cast(const void* src, int src_dtype, int64_t rows, int64_t cols, int64_t ld_src,
              void* dst, int dst_dtype, int64_t ld_dst, void* dst_t, int64_t ld_dst_t,

@@ -99,11 +99,15 @@ def test_dgrad(L, rung, xdt, shape):
     amax = torch.zeros(1, device="cuda")
     flag = torch.zeros(1, dtype=torch.int32, device="cuda")
     L.check(L.lib().apa_linear_dgrad(rung, DY.data_ptr(), DY.stride(0), WT.data_ptr(), WT.stride(0), dx.data_ptr(),
-                                     L.dt_code(xdt), K, M, K, N, amax.data_ptr(), flag.data_ptr(),
+                                     L.dt_code(xdt), K, M, N, K, amax.data_ptr(), flag.data_ptr(),
                                      L.stream_handle()), "dgrad")
     torch.cuda.synchronize()
     got = dx.float().cpu().numpy()
-    assert rel(got, ref) < TOL[rung], rel(got, ref)
+    # dx is delivered in x's dtype: allow one rounding step of that dtype on
+    # top of the rung's tolerance (a last-bit difference of the fp32 sum can
+    # round to the neighbouring bf16/fp16 value)
+    out_step = {torch.bfloat16: 4e-3, torch.float16: 1e-3, torch.float32: 0.0}[xdt]
+    assert rel(got, ref) < TOL[rung] + out_step, rel(got, ref)
     ref_amax, _ = O.track(0.0, 0, work)
     assert amax.item() == pytest.approx(ref_amax, rel=0.13 if rung == 0 else 1e-3)
     assert flag.item() == 0
