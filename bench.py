@@ -254,7 +254,9 @@ def time_gemm(torch, _lib, lin, xr, dev, pk):
             "frac": round(achieved / pk["fp8_tflops"], 4), "us_per_launch": round(us, 2),
             "peak_note": f"2 x {pk['source']} bf16 cuBLAS burst ({pk['bf16_tflops']} TFLOP/s); "
                          "spec dense FP8 4500 TFLOP/s",
-            "traffic": None}
+            # dram__bytes_read.sum + dram__bytes_write.sum of this kernel from one ncu
+            # capture (profiles/gemm_fp8_fwd_8192x4096x4096.md), bytes per launch
+            "traffic": 131.9e6}
 
 
 def run_e2e(torch, make, x, dy32, dev, args, world, barrier, max_over_ranks):
@@ -386,6 +388,55 @@ def run_reference(args):
             "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+def profile_case(case: str):
+    """A few launches of one kernel at the bench shape, for ncu captures:
+    gemm-fp8 / gemm-fp16 / gemm-tf32 (forward GEMM), cast (bf16 x -> E4M3 and
+    its transposed copy), dyprep (fp32 dy -> E4M3 + transposed + bias partials)."""
+    sys.path.insert(0, PKG)
+    import torch
+    from apa import _lib
+    lib = _lib.lib()
+    dev = torch.device("cuda", 0)
+    st = _lib.stream_handle(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    if case.startswith("gemm"):
+        rung = {"gemm-fp8": 0, "gemm-fp16": 1, "gemm-tf32": 2}[case]
+        dt = {0: torch.float8_e4m3fn, 1: torch.float16, 2: torch.float32}[rung]
+        x = torch.randn(M, K, device=dev, generator=g).to(dt)
+        w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(dt)
+        y = torch.empty(M, N, device=dev, dtype=torch.float16 if rung == 1 else torch.float32)
+        amax = torch.zeros(1, device=dev)
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        for _ in range(3):
+            _lib.check(lib.apa_linear_fwd(rung, x.data_ptr(), K, w.data_ptr(), K, None, y.data_ptr(), N, M, N, K,
+                                          amax.data_ptr(), flag.data_ptr(), st), "fwd")
+    elif case == "cast":
+        x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+        xq = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=dev)
+        xqt = torch.empty(K, M, dtype=torch.float8_e4m3fn, device=dev)
+        amax = torch.zeros(1, device=dev)
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        for _ in range(3):
+            _lib.check(lib.apa_cast(x.data_ptr(), _lib.DT_BF16, M, K, K, xq.data_ptr(), _lib.DT_E4M3, K,
+                                    xqt.data_ptr(), M, amax.data_ptr(), flag.data_ptr(), 0, None, None, st), "cast")
+    elif case == "dyprep":
+        dy = torch.randn(M, N, device=dev, generator=g)
+        dq = torch.empty(M, N, dtype=torch.float8_e4m3fn, device=dev)
+        dqt = torch.empty(N, M, dtype=torch.float8_e4m3fn, device=dev)
+        part = torch.empty(M // 64, N, device=dev)
+        amax = torch.zeros(1, device=dev)
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        for _ in range(3):
+            _lib.check(lib.apa_cast(dy.data_ptr(), _lib.DT_F32, M, N, N, dq.data_ptr(), _lib.DT_E4M3, N,
+                                    dqt.data_ptr(), M, amax.data_ptr(), flag.data_ptr(), 1, None, part.data_ptr(),
+                                    st), "dyprep")
+    else:
+        raise SystemExit(f"unknown profile case {case}")
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    print(json.dumps({"profile_case": case, "ok": True}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -393,7 +444,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", default=None,
+                    help="run a few launches of one kernel for an ncu capture (gemm-fp8|gemm-fp16|gemm-tf32|cast|dyprep)")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args.profile_case)
+        return
     if args.warmup < 3:
         args.warmup = 3
     out = run_reference(args) if args.impl == "reference" else run_ours(args)
