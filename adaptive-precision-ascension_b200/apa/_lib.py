@@ -15,7 +15,7 @@ import torch
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libapa_kernels.so")
 
-OK, ERR_INVALID, ERR_ALIGN, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3, 4
+OK, ERR_INVALID, ERR_ALIGN, ERR_UNSUPPORTED, ERR_CUDA, ERR_NOALLOC_LIMIT = 0, 1, 2, 3, 4, 5
 DT_F32, DT_F16, DT_BF16, DT_E4M3, DT_TF32 = 0, 1, 2, 3, 4
 RUNG_FP8, RUNG_FP16, RUNG_TF32 = 0, 1, 2
 EPI_FWD, EPI_DGRAD, EPI_WGRAD = 0, 1, 2
@@ -39,6 +39,7 @@ SIGNATURES = {
     "apa_linear_dgrad": [_I, _VP, _I64, _VP, _I64, _VP, _I, _I64, _I64, _I64, _I64, _VP, _VP, _VP],
     "apa_linear_wgrad": [_I, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _I64, _I, _VP, _VP, _VP],
     "apa_gemm_tn": [_I, _I, _VP, _I64, _VP, _I64, _VP, _I, _I64, _I64, _I64, _I64, _I, _I, _VP],
+    "apa_bias_grad_noalloc": [_VP, _I, _I64, _I64, _I64, _I, _VP, _I, _VP],
     "apa_ladder_pack": [_I, _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP],
     "apa_ladder_eval": [_I, _VP, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _I64, _I64,
                         ctypes.c_double, ctypes.c_double, _VP, _VP],

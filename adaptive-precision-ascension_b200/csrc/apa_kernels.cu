@@ -4,3 +4,4 @@
 #include "cast.cu"
 #include "gemm.cu"
 #include "ladder.cu"
+#include "noalloc.cu"

@@ -181,6 +181,8 @@ extern "C" const char* apa_status_string(int status) {
     case APA_ERR_ALIGN: return "operand not 16-byte aligned for the TMA path";
     case APA_ERR_UNSUPPORTED: return "unsupported dtype or rung";
     case APA_ERR_CUDA: return "CUDA launch or driver error";
+    case APA_ERR_NOALLOC_LIMIT:
+      return "problem exceeds the no-allocation scratch (ceil(rows/64) * cols must be <= 4194304)";
     default: return "unknown status";
   }
 }

@@ -24,6 +24,7 @@ extern "C" {
 #define APA_ERR_ALIGN 2       /* operand not 16-byte aligned where the TMA path needs it */
 #define APA_ERR_UNSUPPORTED 3 /* dtype / rung combination not provided */
 #define APA_ERR_CUDA 4        /* launch failure or missing driver entry point */
+#define APA_ERR_NOALLOC_LIMIT 5 /* problem larger than apa_bias_grad_noalloc's fixed scratch */
 
 /* element types */
 #define APA_DT_F32 0
@@ -163,6 +164,25 @@ int apa_linear_wgrad(int rung, const void* dyqt, int64_t lddyt, const void* xqt,
 int apa_gemm_tn(int rung, int epilogue, const void* A, int64_t lda, const void* B, int64_t ldb,
                 void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
                 int tile_n, int grid_cap, void* stream);
+
+/*
+ * Bias gradient without any device allocation: db[c] = f32(cast(sum_r
+ * f32(cast(dy[r, c], work)), work)) (or += when accumulate != 0), the same
+ * result as apa_cast with colsum_partial followed by apa_colsum_finalize.
+ * No counterpart in the reference: this entry point exists for callers that
+ * cannot allocate device memory when they call (a host framework that owns
+ * all device memory, code running amid another runtime's queued stream work
+ * where cudaMalloc/cudaFree would synchronise the device, foreign-language
+ * bindings holding only borrowed device pointers). Its partial sums live in a
+ * fixed 16 MiB array inside the library, kept by every GPU that loads it:
+ * ceil(rows / 64) * cols must not exceed 4 Mi (else APA_ERR_NOALLOC_LIMIT).
+ * All calls share that array, so calls that overlap on the GPU race; the first
+ * call on a device looks up the array's device address and should come before
+ * any stream capture. It calls no cudaMalloc/cudaFree.
+ * dy_dtype: F32, F16 or BF16; work_dtype: E4M3, F16 or F32.
+ */
+int apa_bias_grad_noalloc(const void* dy, int dy_dtype, int64_t rows, int64_t cols, int64_t ld,
+                          int work_dtype, float* db, int accumulate, void* stream);
 
 /*
  * Ladder evaluation on device, one launch per step.
