@@ -114,6 +114,48 @@ __device__ __forceinline__ uint16_t e4m3_to_f16(uint32_t b) {
   return f16_from_f32(e4m3_to_f32(b));
 }
 
+// ---------------------------------------------------------------------------
+// Paired hardware conversions. The E4M3 one saturates (|x| > 448 -> 448, Inf
+// -> 448, NaN -> NaN); callers apply the non-saturating rule of the reference
+// (|x| > 464, Inf and NaN -> 0x7F | sign) wherever a value above 464 or a
+// non-finite value can occur; below that the hardware's round-to-nearest-even
+// equals e4m3_from_f32.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kE4M3NaNThresholdBits = 0x43E80000u;   // 464.0f
+
+// {lo, hi} -> 16 bits: lo's code in bits 0-7, hi's in bits 8-15 (saturating)
+__device__ __forceinline__ uint32_t e4m3x2_sat(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// {lo, hi} -> 16 bits with the reference's non-saturating rule applied to both
+__device__ __forceinline__ uint32_t e4m3x2_exact(float lo, float hi) {
+  uint32_t r = e4m3x2_sat(lo, hi);
+  const uint32_t ul = __float_as_uint(lo), uh = __float_as_uint(hi);
+  if ((ul & 0x7FFFFFFFu) > kE4M3NaNThresholdBits) r = (r & 0xFF00u) | 0x7Fu | ((ul >> 24) & 0x80u);
+  if ((uh & 0x7FFFFFFFu) > kE4M3NaNThresholdBits) r = (r & 0x00FFu) | 0x7F00u | ((uh >> 16) & 0x8000u);
+  return r;
+}
+
+// two E4M3 codes (bits 0-7, 8-15) -> two binary16 values (exact) in one word
+__device__ __forceinline__ uint32_t f16x2_from_e4m3x2(uint32_t codes) {
+  uint32_t r;
+  asm("{\n\t.reg .b16 t;\n\tmov.b16 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(r) : "h"((uint16_t)codes));
+  return r;
+}
+
+// {lo, hi} fp32 -> binary16 pair (round to nearest even), lo in bits 0-15
+__device__ __forceinline__ uint32_t f16x2_from_f32(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ float f16lo_to_f32(uint32_t w) { return __half2float(__ushort_as_half((uint16_t)(w & 0xFFFFu))); }
+__device__ __forceinline__ float f16hi_to_f32(uint32_t w) { return __half2float(__ushort_as_half((uint16_t)(w >> 16))); }
+
 // |v| as fp32 bits: comparing these as unsigned integers orders magnitudes
 // with every NaN above +Inf, which is the NaN-propagating max torch.max uses.
 __device__ __forceinline__ uint32_t mag_bits(float v) {

@@ -130,129 +130,239 @@ struct CastParams {
 };
 
 template <int SRC, int DST>
-__global__ void __launch_bounds__(kThreads) cast_kernel(CastParams p) {
-  __shared__ uint32_t tile[kTile][kTile + 1];
+__global__ void __launch_bounds__(kThreads, 4) cast_kernel(CastParams p) {
+  // 64 x 64 tile per iteration; thread t owns the 4 x 4 block at rows 4a..4a+3,
+  // columns 4b..4b+3 (a = t / 16, b = t % 16). The transposed copy goes
+  // through shared memory as packed column strips of 4 codes.
+  constexpr int ES = Elem<DST>::bytes;
+  constexpr int PITCH = 64 * ES + 4;   // bytes per transposed row; the 4-byte pad spreads banks
+  __shared__ __align__(16) uint8_t tileT[64 * PITCH];
+  __shared__ float csum_s[8][64];
   __shared__ uint32_t red[kThreads / 32];
-  const int tid = threadIdx.x;
-  const int r_in = tid >> 2;               // tile row handled in the load phase
-  const int c_in = (tid & 3) * kSeg;       // first tile column of this thread's segment
+  const int t = threadIdx.x;
+  const int a = t >> 4, b = t & 15;
+  const int warp = t >> 5, lane = t & 31;
   const int64_t tiles_r = (p.rows + kTile - 1) / kTile;
   const int64_t tiles_c = (p.cols + kTile - 1) / kTile;
   const int64_t ntiles = tiles_r * tiles_c;
   const bool stage = (p.dst_t != nullptr) || (p.colsum != nullptr);
-  uint32_t mag = 0;
+  uint32_t msrc = 0;   // max |source value| (fp32 bits) over in-bounds elements
 
-  for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
-    const int64_t tr = t / tiles_c, tc = t - tr * tiles_c;
-    const int64_t row = tr * kTile + r_in;
-    const int64_t col0 = tc * kTile + c_in;
-    uint32_t code[kSeg];
-    const bool row_ok = row < p.rows;
-    const bool full = row_ok && (col0 + kSeg <= p.cols);
-    float v[kSeg];
-    if (full && p.vec_src) {
-      const int64_t off = row * p.ld_src + col0;
-      if constexpr (Elem<SRC>::bytes == 4) {
-        const float4* s = reinterpret_cast<const float4*>(static_cast<const float*>(p.src) + off);
+  for (int64_t tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int64_t tr = tile / tiles_c, tc = tile - tr * tiles_c;
+    const int64_t r0 = tr * kTile + 4 * a;
+    const int64_t c0 = tc * kTile + 4 * b;
+    const bool cols_full = c0 + 4 <= p.cols;
+    float v[4][4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float4 w = __ldg(s + q);
-          v[4 * q] = w.x; v[4 * q + 1] = w.y; v[4 * q + 2] = w.z; v[4 * q + 3] = w.w;
-        }
-      } else if constexpr (Elem<SRC>::bytes == 2) {
-        const uint4* s = reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.src) + off);
+    for (int i = 0; i < 4; ++i) {
+      const int64_t row = r0 + i;
+      const bool row_ok = row < p.rows;
+      if (row_ok && cols_full && p.vec_src) {
+        const int64_t off = row * p.ld_src + c0;
+        if constexpr (Elem<SRC>::bytes == 4) {
+          const float4 w = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(p.src) + off));
+          v[i][0] = w.x; v[i][1] = w.y; v[i][2] = w.z; v[i][3] = w.w;
+        } else {
+          const uint2 w = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p.src) + off));
+          const uint32_t ws[2] = {w.x, w.y};
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          uint4 w = __ldg(s + q);
-          uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
+          for (int h = 0; h < 2; ++h) {
             if constexpr (SRC == APA_DT_BF16) {
-              v[8 * q + 2 * h] = bf16_to_f32((uint16_t)(ws[h] & 0xFFFF));
-              v[8 * q + 2 * h + 1] = bf16_to_f32((uint16_t)(ws[h] >> 16));
+              v[i][2 * h] = bf16_to_f32((uint16_t)(ws[h] & 0xFFFFu));
+              v[i][2 * h + 1] = bf16_to_f32((uint16_t)(ws[h] >> 16));
             } else {
-              v[8 * q + 2 * h] = f16_to_f32((uint16_t)(ws[h] & 0xFFFF));
-              v[8 * q + 2 * h + 1] = f16_to_f32((uint16_t)(ws[h] >> 16));
+              v[i][2 * h] = f16_to_f32((uint16_t)(ws[h] & 0xFFFFu));
+              v[i][2 * h + 1] = f16_to_f32((uint16_t)(ws[h] >> 16));
             }
           }
         }
       } else {
-        const uint4 w = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.src) + off));
-        uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int j = 0; j < kSeg; ++j) v[j] = e4m3_to_f32((ws[j >> 2] >> (8 * (j & 3))) & 0xFF);
+        for (int j = 0; j < 4; ++j)
+          v[i][j] = (row_ok && c0 + j < p.cols) ? load_as_f32<SRC>(p.src, row * p.ld_src + c0 + j) : 0.0f;
       }
+    }
+    // telemetry on the source magnitudes (out-of-bounds slots hold +0)
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) msrc = max(msrc, mag_bits(v[i][j]));
+
+    // encode
+    uint32_t code[4][4];
+    if constexpr (DST == APA_DT_E4M3) {
+      uint32_t m = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) m = max(m, mag_bits(v[i][j]));
+      const bool big = m > kE4M3NaNThresholdBits;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; j += 2) {
+          const uint32_t w = big ? e4m3x2_exact(v[i][j], v[i][j + 1]) : e4m3x2_sat(v[i][j], v[i][j + 1]);
+          code[i][j] = w & 0xFFu;
+          code[i][j + 1] = w >> 8;
+        }
+    } else if constexpr (DST == APA_DT_F16) {
+      uint32_t m = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) m = max(m, mag_bits(v[i][j]));
+      if (m > 0x7F800000u) {   // a NaN: keep its sign and payload as torch does
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) code[i][j] = f16_from_f32(v[i][j]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; j += 2) {
+            const uint32_t w = f16x2_from_f32(v[i][j], v[i][j + 1]);
+            code[i][j] = w & 0xFFFFu;
+            code[i][j + 1] = w >> 16;
+          }
+      }
+    } else if constexpr (DST == APA_DT_BF16) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) code[i][j] = bf16_from_f32(v[i][j]);
     } else {
 #pragma unroll
-      for (int j = 0; j < kSeg; ++j)
-        v[j] = (row_ok && col0 + j < p.cols) ? load_as_f32<SRC>(p.src, row * p.ld_src + col0 + j) : 0.0f;
-    }
+      for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < kSeg; ++j) {
-      code[j] = encode<SRC, DST>(v[j]);
-      const bool in = row_ok && (col0 + j < p.cols);
-      if (in) mag = max(mag, p.telem_on_source ? mag_bits(v[j]) : code_mag_bits<DST>(code[j]));
+        for (int j = 0; j < 4; ++j) code[i][j] = __float_as_uint(v[i][j]);
     }
+
+    // row-major copy (TF32 operands rounded on the way out)
     if (p.dst) {
-      uint32_t out[kSeg];
 #pragma unroll
-      for (int j = 0; j < kSeg; ++j) {
-        if constexpr (DST == APA_DT_F32) out[j] = p.tf32 ? tf32_rn_bits(code[j]) : code[j];
-        else out[j] = code[j];
-      }
-      if (full) {
-        store16<DST>(p.dst, row * p.ld_dst + col0, out, p.vec_dst != 0);
-      } else if (row_ok) {
+      for (int i = 0; i < 4; ++i) {
+        const int64_t row = r0 + i;
+        if (row >= p.rows) continue;
+        uint32_t o[4];
 #pragma unroll
-        for (int j = 0; j < kSeg; ++j)
-          if (col0 + j < p.cols) store_code<DST>(p.dst, row * p.ld_dst + col0 + j, out[j]);
-      }
-    }
-    if (stage) {
-#pragma unroll
-      for (int j = 0; j < kSeg; ++j) {
-        const bool in = row_ok && (col0 + j < p.cols);
-        tile[r_in][c_in + j] = in ? code[j] : 0u;   // code 0 is +0 in every dtype
-      }
-      __syncthreads();
-      // transposed phase: thread handles tile column jc, rows rs..rs+15
-      const int jc = tid >> 2;
-      const int rs = (tid & 3) * kSeg;
-      const int64_t tcol = tc * kTile + jc;          // source column = transposed row
-      const int64_t trow0 = tr * kTile + rs;         // source row = transposed column
-      uint32_t tcode[kSeg];
-      float csum = 0.0f;
-#pragma unroll
-      for (int i = 0; i < kSeg; ++i) {
-        tcode[i] = tile[rs + i][jc];
-        csum += decode<DST>(tcode[i]);
-        if constexpr (DST == APA_DT_F32) tcode[i] = p.tf32 ? tf32_rn_bits(tcode[i]) : tcode[i];
-      }
-      if (p.dst_t && tcol < p.cols) {
-        if (trow0 + kSeg <= p.rows) {
-          store16<DST>(p.dst_t, tcol * p.ld_dst_t + trow0, tcode, p.vec_dst_t != 0);
+        for (int j = 0; j < 4; ++j) {
+          if constexpr (DST == APA_DT_F32) o[j] = p.tf32 ? tf32_rn_bits(code[i][j]) : code[i][j];
+          else o[j] = code[i][j];
+        }
+        const int64_t off = row * p.ld_dst + c0;
+        if (cols_full && p.vec_dst) {
+          if constexpr (ES == 1)
+            *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(p.dst) + off) = o[0] | (o[1] << 8) | (o[2] << 16) | (o[3] << 24);
+          else if constexpr (ES == 2)
+            *reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.dst) + off) = make_uint2(o[0] | (o[1] << 16), o[2] | (o[3] << 16));
+          else
+            *reinterpret_cast<uint4*>(static_cast<uint32_t*>(p.dst) + off) = make_uint4(o[0], o[1], o[2], o[3]);
         } else {
 #pragma unroll
-          for (int i = 0; i < kSeg; ++i)
-            if (trow0 + i < p.rows) store_code<DST>(p.dst_t, tcol * p.ld_dst_t + trow0 + i, tcode[i]);
+          for (int j = 0; j < 4; ++j)
+            if (c0 + j < p.cols) store_code<DST>(p.dst, off + j, o[j]);
+        }
+      }
+    }
+
+    if (stage) {
+      // column strips: codes of rows 4a..4a+3 of column 4b+c, packed, at
+      // transposed row (4b + c), byte offset 4a*ES
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint8_t* dstT = tileT + (4 * b + c) * PITCH + 4 * a * ES;
+        if constexpr (ES == 1) {
+          *reinterpret_cast<uint32_t*>(dstT) =
+              code[0][c] | (code[1][c] << 8) | (code[2][c] << 16) | (code[3][c] << 24);
+        } else if constexpr (ES == 2) {
+          reinterpret_cast<uint32_t*>(dstT)[0] = code[0][c] | (code[1][c] << 16);
+          reinterpret_cast<uint32_t*>(dstT)[1] = code[2][c] | (code[3][c] << 16);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) reinterpret_cast<uint32_t*>(dstT)[i] = code[i][c];
         }
       }
       if (p.colsum) {
-        csum += __shfl_xor_sync(0xFFFFFFFFu, csum, 1);
-        csum += __shfl_xor_sync(0xFFFFFFFFu, csum, 2);
-        if ((tid & 3) == 0 && tcol < p.cols) p.colsum[tr * p.cols + tcol] = csum;
+        // partial column sums of the cast values over this thread's 4 rows,
+        // then over the 16 threads sharing b (lanes b and b+16 of each warp,
+        // then the 8 warps in a fixed order)
+        float cs[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float s = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) s += decode<DST>(code[i][c]);
+          cs[c] = s + __shfl_xor_sync(0xFFFFFFFFu, s, 16);
+        }
+        if (lane < 16) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) csum_s[warp][4 * b + c] = cs[c];
+        }
+      }
+      __syncthreads();
+      if (p.colsum && t < 64) {
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) s += csum_s[w][t];
+        const int64_t col = tc * kTile + t;
+        if (col < p.cols) p.colsum[tr * p.cols + col] = s;
+      }
+      if (p.dst_t) {
+        // transposed rows: 64 x (64*ES bytes) = 256*ES chunks of 16 bytes
+#pragma unroll
+        for (int k = 0; k < ES; ++k) {
+          const int id = t + kThreads * k;
+          const int j = id / (4 * ES);           // transposed row in the tile (source column)
+          const int ch = id - j * (4 * ES);      // 16-byte chunk within that row
+          const int64_t orow = tc * kTile + j;
+          if (orow >= p.cols) continue;
+          const uint32_t* s = reinterpret_cast<const uint32_t*>(tileT + j * PITCH + ch * 16);
+          uint32_t w[4] = {s[0], s[1], s[2], s[3]};
+          if constexpr (DST == APA_DT_F32) {
+            if (p.tf32) {
+#pragma unroll
+              for (int h = 0; h < 4; ++h) w[h] = tf32_rn_bits(w[h]);
+            }
+          }
+          constexpr int PER = 16 / ES;            // elements per chunk
+          const int64_t ocol = tr * kTile + ch * PER;
+          const int64_t off = orow * p.ld_dst_t + ocol;
+          if (ocol + PER <= p.rows && p.vec_dst_t) {
+            *reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.dst_t) + off * ES) = make_uint4(w[0], w[1], w[2], w[3]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < PER; ++e) {
+              if (ocol + e < p.rows) {
+                uint32_t cval;
+                if constexpr (ES == 1) cval = (w[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+                else if constexpr (ES == 2) cval = (w[e >> 1] >> (16 * (e & 1))) & 0xFFFFu;
+                else cval = w[e];
+                store_code<DST>(p.dst_t, off + e, cval);
+              }
+            }
+          }
+        }
       }
       __syncthreads();
     }
   }
-  // block reduction of the magnitude, one atomic per block
+  // telemetry: the cast values' max is the cast of the source max (rounding
+  // to E4M3 / fp16 is monotone in magnitude, NaN rule included)
+  uint32_t mag = msrc;
+  if (!p.telem_on_source) {
+    if constexpr (DST == APA_DT_E4M3) mag = e4m3_mag_bits(e4m3_from_f32(__uint_as_float(msrc)));
+    else if constexpr (DST == APA_DT_F16) mag = mag_bits(f16_to_f32(f16_from_f32(__uint_as_float(msrc))));
+    else if constexpr (DST == APA_DT_BF16) mag = mag_bits(bf16_to_f32(bf16_from_f32(__uint_as_float(msrc))));
+  }
   mag = warp_max_u32(mag);
-  if ((tid & 31) == 0) red[tid >> 5] = mag;
+  if (lane == 0) red[warp] = mag;
   __syncthreads();
-  if (tid < 32) {
-    uint32_t m = tid < kThreads / 32 ? red[tid] : 0u;
+  if (t < 32) {
+    uint32_t m = t < kThreads / 32 ? red[t] : 0u;
     m = warp_max_u32(m);
-    if (tid == 0) {
+    if (t == 0) {
       telem_commit(p.amax, p.flag, m);
       if (blockIdx.x == 0 && p.merge_amax) telem_commit(p.amax, p.flag, mag_bits(*p.merge_amax));
     }
@@ -349,17 +459,28 @@ __global__ void __launch_bounds__(256) underflow_kernel(const void* src, int64_t
 // Bias gradient: sum the per-64-row partials in a fixed order, round to the
 // working dtype (the autograd engine's cast to bias_work's dtype) and widen
 // to fp32 for bias_master.grad (manager.py:200-204).
-__global__ void colsum_finalize_kernel(const float* partial, int64_t nparts, int64_t cols, int work_dt,
-                                       float* out, int accumulate) {
-  const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= cols) return;
+__global__ void __launch_bounds__(256) colsum_finalize_kernel(const float* partial, int64_t nparts, int64_t cols,
+                                                              int work_dt, float* out, int accumulate) {
+  // block: 32 columns x 8 warps; warp w sums partial rows w, w+8, ... in
+  // order, then warp 0 adds the 8 warp sums in order (deterministic)
+  __shared__ float part[8][32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t c = (int64_t)blockIdx.x * 32 + lane;
   float s = 0.0f;
-  for (int64_t r = 0; r < nparts; ++r) s += partial[r * cols + c];
-  float q;
-  if (work_dt == APA_DT_E4M3) q = e4m3_to_f32(e4m3_from_f32(s));
-  else if (work_dt == APA_DT_F16) q = f16_to_f32(f16_from_f32(s));
-  else q = s;
-  out[c] = accumulate ? out[c] + q : q;
+  if (c < cols)
+    for (int64_t r = w; r < nparts; r += 8) s += partial[r * cols + c];
+  part[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && c < cols) {
+    float t = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += part[k][lane];
+    float q;
+    if (work_dt == APA_DT_E4M3) q = e4m3_to_f32(e4m3_from_f32(t));
+    else if (work_dt == APA_DT_F16) q = f16_to_f32(f16_from_f32(t));
+    else q = t;
+    out[c] = accumulate ? out[c] + q : q;
+  }
 }
 
 // Zero a list of int32 words (per-step flag reset, manager.py:161-168).
@@ -371,7 +492,7 @@ __global__ void zero_list_kernel(int* const* ptrs, int n) {
 template <int SRC, int DST>
 int launch_cast_t(CastParams& p, cudaStream_t s) {
   const int64_t tiles = ((p.rows + kTile - 1) / kTile) * ((p.cols + kTile - 1) / kTile);
-  int64_t grid = std::min<int64_t>(tiles, (int64_t)num_sms() * 8);
+  int64_t grid = std::min<int64_t>(tiles, (int64_t)num_sms() * 4);
   if (grid < 1) grid = 1;
   cast_kernel<SRC, DST><<<(unsigned)grid, kThreads, 0, s>>>(p);
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
@@ -482,7 +603,7 @@ extern "C" int apa_colsum_finalize(const float* partial, int64_t nparts, int64_t
                                    float* out, int accumulate, void* stream) {
   if (!partial || !out || nparts < 0 || cols < 0) return APA_ERR_INVALID;
   if (cols == 0) return APA_OK;
-  const unsigned grid = (unsigned)((cols + 255) / 256);
+  const unsigned grid = (unsigned)((cols + 31) / 32);
   colsum_finalize_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(partial, nparts, cols, work_dtype,
                                                                               out, accumulate);
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;

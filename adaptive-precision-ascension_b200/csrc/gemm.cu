@@ -54,6 +54,8 @@ template <> struct KindInfo<KIND_E4M3> { static constexpr int bytes = 1; static 
 template <> struct KindInfo<KIND_F16> { static constexpr int bytes = 2; static constexpr uint32_t fmt = 0; };
 template <> struct KindInfo<KIND_TF32> { static constexpr int bytes = 4; static constexpr uint32_t fmt = 2; };
 
+constexpr int kEpiStageBytes = 4096;   // per epilogue warp: 32 rows x 128 bytes of output
+
 template <int BN> struct Cfg {
   static constexpr int kStages = BN == 256 ? 4 : 6;
   static constexpr int kABytes = BM * kSlab;
@@ -61,11 +63,14 @@ template <int BN> struct Cfg {
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
+  static constexpr int kEpiBytes = 4 * kEpiStageBytes + 4 * BN * 4;   // staging + per-warp bias
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + kBarrierBytes + 1024;
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
 
 struct EpiArgs {
   void* out; int64_t ldo; int out_dt; int vec_out;
+  int tma_out;                      // output written by TMA bulk-tensor stores
   const void* bias;                 // FWD: working-dtype bias (nullable)
   float* amax; int* flag;           // FWD: module telemetry; DGRAD: boundary_cast telemetry
   unsigned long long* counters;     // WGRAD: [nonzero, underflow, ticket], zero on entry
@@ -195,117 +200,213 @@ __device__ __forceinline__ float bias_value(const void* bias, int n) {
   else return static_cast<const float*>(bias)[n];
 }
 
-// Write 32 fp32 values (as bits) of one row; cnt valid columns.
-__device__ __forceinline__ void store_row(const EpiArgs& ea, int row, int col0, int cnt, const uint32_t (&w)[32],
-                                          int out_dt) {
-  if (out_dt == APA_DT_F32) {
-    float* o = static_cast<float*>(ea.out) + (int64_t)row * ea.ldo + col0;
-    if (cnt == 32 && ea.vec_out) {
+__device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tm)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t bf16x2_from_f32(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ float fu(uint32_t u) { return __uint_as_float(u); }
+
+struct EpiState {
+  uint32_t mag = 0;          // max |value| as fp32 bits, before the output rounding
+  uint32_t nz = 0, uf = 0;   // WGRAD counters
+};
+
+// Telemetry reductions are taken on the unrounded fp32 values: rounding to
+// E4M3 / fp16 is monotone in magnitude (including the NaN rule above 464),
+// so max |round(v)| = round(max |v|) and one conversion at the end suffices.
+__device__ __forceinline__ uint32_t chunk_max(const uint32_t* r, int n, bool check, bool row_ok, int nv) {
+  uint32_t m = 0;
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        reinterpret_cast<uint4*>(o)[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  for (int j = 0; j < 64; ++j) {
+    if (j < n) {
+      const uint32_t a = r[j] & 0x7FFFFFFFu;
+      if (!check || (row_ok && j < nv)) m = max(m, a);
+    }
+  }
+  return m;
+}
+
+// One 64-column unit of one row: r[0..63] hold the fp32 accumulators on
+// entry and the output words on exit (64 fp32 words, or 32 words of packed
+// 16-bit pairs). check: the tile is ragged, mask telemetry with row_ok / nv.
+template <int KIND, int EPI>
+__device__ __forceinline__ void epi_unit(const EpiArgs& ea, const float* sb, uint32_t (&r)[64], EpiState& st,
+                                         bool check, bool row_ok, int nv) {
+  if constexpr (EPI == EPI_FWD) {
+    if (ea.bias != nullptr) {
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        const float4 b = reinterpret_cast<const float4*>(sb)[q];
+        r[4 * q + 0] = __float_as_uint(fu(r[4 * q + 0]) + b.x);
+        r[4 * q + 1] = __float_as_uint(fu(r[4 * q + 1]) + b.y);
+        r[4 * q + 2] = __float_as_uint(fu(r[4 * q + 2]) + b.z);
+        r[4 * q + 3] = __float_as_uint(fu(r[4 * q + 3]) + b.w);
+      }
+    }
+    st.mag = max(st.mag, chunk_max(r, 64, check, row_ok, nv));
+    if constexpr (KIND == KIND_F16) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) r[k] = f16x2_from_f32(fu(r[2 * k]), fu(r[2 * k + 1]));
+    }
+  } else if constexpr (EPI == EPI_DGRAD) {
+    const uint32_t m = chunk_max(r, 64, check, row_ok, nv);
+    st.mag = max(st.mag, m);
+    const int od = ea.out_dt;
+    if constexpr (KIND == KIND_E4M3) {
+      const bool big = __any_sync(0xFFFFFFFFu, m > kE4M3NaNThresholdBits);
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const float v0 = fu(r[2 * k]), v1 = fu(r[2 * k + 1]);
+        const uint32_t h = f16x2_from_e4m3x2(big ? e4m3x2_exact(v0, v1) : e4m3x2_sat(v0, v1));
+        if (od == APA_DT_F16) {
+          r[k] = h;
+        } else {
+          const float f0 = f16lo_to_f32(h), f1 = f16hi_to_f32(h);
+          if (od == APA_DT_BF16) {
+            r[k] = (__float_as_uint(f0) >> 16) | (__float_as_uint(f1) & 0xFFFF0000u);   // exact
+          } else {
+            r[2 * k] = __float_as_uint(f0);
+            r[2 * k + 1] = __float_as_uint(f1);
+          }
+        }
+      }
+    } else if constexpr (KIND == KIND_F16) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const uint32_t h = f16x2_from_f32(fu(r[2 * k]), fu(r[2 * k + 1]));
+        if (od == APA_DT_F16) {
+          r[k] = h;
+        } else if (od == APA_DT_BF16) {
+          r[k] = bf16x2_from_f32(f16lo_to_f32(h), f16hi_to_f32(h));
+        } else {
+          r[2 * k] = __float_as_uint(f16lo_to_f32(h));
+          r[2 * k + 1] = __float_as_uint(f16hi_to_f32(h));
+        }
+      }
     } else {
+      if (od == APA_DT_BF16) {
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (j < cnt) o[j] = __uint_as_float(w[j]);
+        for (int k = 0; k < 32; ++k) r[k] = bf16x2_from_f32(fu(r[2 * k]), fu(r[2 * k + 1]));
+      } else if (od == APA_DT_F16) {
+#pragma unroll
+        for (int k = 0; k < 32; ++k) r[k] = f16x2_from_f32(fu(r[2 * k]), fu(r[2 * k + 1]));
+      }
     }
   } else {
-    // 16-bit outputs: w holds the 16-bit codes
-    uint16_t* o = static_cast<uint16_t*>(ea.out) + (int64_t)row * ea.ldo + col0;
-    if (cnt == 32 && ea.vec_out) {
+    const uint32_t vb = __float_as_uint(ea.vmin);
+    if constexpr (KIND == KIND_E4M3) {
+      const uint32_t m = chunk_max(r, 64, check, row_ok, nv);
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        reinterpret_cast<uint4*>(o)[q] =
-            make_uint4(w[8 * q] | (w[8 * q + 1] << 16), w[8 * q + 2] | (w[8 * q + 3] << 16),
-                       w[8 * q + 4] | (w[8 * q + 5] << 16), w[8 * q + 6] | (w[8 * q + 7] << 16));
-    } else {
+      for (int j = 0; j < 64; ++j) {
+        // nonzero: 0 < |v| <= Inf (NaN excluded); underflow: nonzero and |v| < vmin
+        const uint32_t a = (r[j] & 0x7FFFFFFFu) - 1u;
+        const bool ok = !check || (row_ok && j < nv);
+        st.nz += (ok && a < 0x7F800000u) ? 1u : 0u;
+        st.uf += (ok && a < vb - 1u) ? 1u : 0u;
+      }
+      const bool big = __any_sync(0xFFFFFFFFu, m > kE4M3NaNThresholdBits);
 #pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (j < cnt) o[j] = (uint16_t)w[j];
+      for (int k = 0; k < 32; ++k) {
+        const float v0 = fu(r[2 * k]), v1 = fu(r[2 * k + 1]);
+        const uint32_t h = f16x2_from_e4m3x2(big ? e4m3x2_exact(v0, v1) : e4m3x2_sat(v0, v1));
+        r[2 * k] = __float_as_uint(f16lo_to_f32(h));
+        r[2 * k + 1] = __float_as_uint(f16hi_to_f32(h));
+      }
+    } else if constexpr (KIND == KIND_F16) {
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        const uint32_t h = f16x2_from_f32(fu(r[2 * k]), fu(r[2 * k + 1]));
+        r[2 * k] = __float_as_uint(f16lo_to_f32(h));
+        r[2 * k + 1] = __float_as_uint(f16hi_to_f32(h));
+      }
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        const uint32_t a = (r[j] & 0x7FFFFFFFu) - 1u;
+        const bool ok = !check || (row_ok && j < nv);
+        st.nz += (ok && a < 0x7F800000u) ? 1u : 0u;
+        st.uf += (ok && a < vb - 1u) ? 1u : 0u;
+      }
     }
   }
 }
 
-struct EpiState {
-  uint32_t mag = 0;
-  uint32_t nz = 0, uf = 0;
-};
-
+// Final telemetry magnitude: the unrounded max passed through the same
+// rounding the stored (or hooked) tensor saw.
 template <int KIND, int EPI>
-__device__ __forceinline__ void epilogue_chunk(const EpiArgs& ea, int row, int col0, uint32_t (&r)[32],
-                                               EpiState& st) {
-  const int cnt = min(32, ea.N - col0);
-  if constexpr (EPI == EPI_FWD) {
+__device__ __forceinline__ uint32_t final_mag(uint32_t mag) {
+  if constexpr (KIND == KIND_E4M3 && EPI == EPI_DGRAD) return e4m3_mag_bits(e4m3_from_f32(__uint_as_float(mag)));
+  else if constexpr (KIND == KIND_F16) return mag_bits(f16_to_f32(f16_from_f32(__uint_as_float(mag))));
+  else return mag;
+}
+
+// Direct (non-TMA) store of one unit: used when the output rows are not
+// 16-byte aligned or when accumulating into the existing gradient.
+__device__ __forceinline__ void store_unit_direct(const EpiArgs& ea, int row, int col0, int nv, uint32_t (&r)[64],
+                                                  bool out16) {
+  if (out16) {
+    uint16_t* o = static_cast<uint16_t*>(ea.out) + (int64_t)row * ea.ldo + col0;
+    if (nv >= 64 && ea.vec_out) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      float v = __uint_as_float(r[j]);
-      if (ea.bias != nullptr && j < cnt) v += bias_value<KIND>(ea.bias, col0 + j);
-      if constexpr (KIND == KIND_F16) {
-        const uint16_t h = f16_from_f32(v);
-        if (j < cnt) st.mag = max(st.mag, mag_bits(f16_to_f32(h)));
-        r[j] = h;
-      } else {
-        if (j < cnt) st.mag = max(st.mag, mag_bits(v));
-        r[j] = __float_as_uint(v);
-      }
-    }
-    store_row(ea, row, col0, cnt, r, KIND == KIND_F16 ? APA_DT_F16 : APA_DT_F32);
-  } else if constexpr (EPI == EPI_DGRAD) {
+      for (int q = 0; q < 8; ++q)
+        reinterpret_cast<uint4*>(o)[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+    } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      const float v = __uint_as_float(r[j]);
-      float qv;          // value after the re-cast to the working dtype
-      uint32_t outc;     // code in the output dtype
-      if constexpr (KIND == KIND_E4M3) {
-        const uint32_t c = e4m3_from_f32(v);
-        qv = e4m3_to_f32(c);
-        if (j < cnt) st.mag = max(st.mag, e4m3_mag_bits(c));
-        outc = ea.out_dt == APA_DT_F16 ? (uint32_t)e4m3_to_f16(c)
-               : ea.out_dt == APA_DT_BF16 ? (__float_as_uint(qv) >> 16)   // exact: 3 mantissa bits
-                                          : __float_as_uint(qv);
-      } else if constexpr (KIND == KIND_F16) {
-        const uint16_t h = f16_from_f32(v);
-        qv = f16_to_f32(h);
-        if (j < cnt) st.mag = max(st.mag, mag_bits(qv));
-        outc = ea.out_dt == APA_DT_F16 ? (uint32_t)h
-               : ea.out_dt == APA_DT_BF16 ? (uint32_t)bf16_from_f32(qv)
-                                          : __float_as_uint(qv);
-      } else {
-        qv = v;
-        if (j < cnt) st.mag = max(st.mag, mag_bits(qv));
-        outc = ea.out_dt == APA_DT_F16 ? (uint32_t)f16_from_f32(qv)
-               : ea.out_dt == APA_DT_BF16 ? (uint32_t)bf16_from_f32(qv)
-                                          : __float_as_uint(qv);
-      }
-      r[j] = outc;
+      for (int j = 0; j < 64; ++j)
+        if (j < nv) o[j] = (uint16_t)((r[j >> 1] >> (16 * (j & 1))) & 0xFFFFu);
     }
-    store_row(ea, row, col0, cnt, r, ea.out_dt);
   } else {
-    const uint32_t vmin_bits = __float_as_uint(ea.vmin);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      float v = __uint_as_float(r[j]);
-      if constexpr (KIND == KIND_F16) v = f16_to_f32(f16_from_f32(v));   // the fp16 GEMM output
-      if constexpr (KIND != KIND_TF32) {
-        // |v| > 0 and |v| < vmin, compared as magnitudes (NaN is neither)
-        const uint32_t m = mag_bits(v);
-        const bool nonzero = m != 0u && m <= 0x7F800000u;
-        if (j < cnt) {
-          st.nz += nonzero ? 1u : 0u;
-          st.uf += (nonzero && m < vmin_bits) ? 1u : 0u;
-        }
-      }
-      float q;
-      if constexpr (KIND == KIND_E4M3) q = e4m3_to_f32(e4m3_from_f32(v));
-      else q = v;
-      r[j] = __float_as_uint(q);
-    }
+    float* o = static_cast<float*>(ea.out) + (int64_t)row * ea.ldo + col0;
     if (ea.accumulate) {
-      const float* o = static_cast<const float*>(ea.out) + (int64_t)row * ea.ldo + col0;
-      for (int j = 0; j < cnt; ++j) r[j] = __float_as_uint(o[j] + __uint_as_float(r[j]));
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        if (j < nv) r[j] = __float_as_uint(o[j] + fu(r[j]));
     }
-    store_row(ea, row, col0, cnt, r, APA_DT_F32);
+    if (nv >= 64 && ea.vec_out) {
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        reinterpret_cast<uint4*>(o)[q] = make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 64; ++j)
+        if (j < nv) o[j] = fu(r[j]);
+    }
   }
+}
+
+// Stage 32 words (128 bytes) of this lane's row into the warp's 4 KB buffer
+// in the 128-byte-swizzled layout the output tensor map expects (16-byte
+// chunk c of row r lands at chunk c ^ (r % 8)): conflict-free stores.
+__device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const uint32_t* w) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    *reinterpret_cast<uint4*>(buf + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+        make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
 }
 
 // ---------------------------------------------------------------------------
@@ -313,7 +414,8 @@ __device__ __forceinline__ void epilogue_chunk(const EpiArgs& ea, int row, int c
 // ---------------------------------------------------------------------------
 template <int KIND, int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, EpiArgs ea) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmO, EpiArgs ea) {
   using C = Cfg<BN>;
   constexpr int kStages = C::kStages;
   constexpr int kElemPerSlab = kSlab / KindInfo<KIND>::bytes;
@@ -322,7 +424,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* smA = smem;
   uint8_t* smB = smem + kStages * C::kABytes;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * C::kStageBytes);
+  uint8_t* sEpi = smem + kStages * C::kStageBytes;                 // 4 warps x 4 KB staging
+  float* sBias = reinterpret_cast<float*>(sEpi + 4 * kEpiStageBytes);   // 4 warps x BN floats
+  uint64_t* full = reinterpret_cast<uint64_t*>(sBias + 4 * BN);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
@@ -409,27 +513,79 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // epilogue warps 2..5 -> TMEM lane quarters 2,3,0,1
     const int q = warp & 3;
+    const int e = warp - 2;
+    uint8_t* stage_buf = sEpi + e * kEpiStageBytes;
+    float* sb = sBias + e * BN;
+    const bool out16 = ea.out_dt != APA_DT_F32;
     EpiState st;
     int local = 0;
+    bool pending_store = false;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
+      const int m_blk = tile / num_n, n_blk = tile - (tile / num_n) * num_n;
+      const int col_base = n_blk * BN;
+      const int row0 = m_blk * BM + q * 32;
+      const int row = row0 + lane;
+      const bool row_ok = row < ea.M;
+      const bool check = (row0 + 32 > ea.M) || (col_base + BN > ea.N);
+      if constexpr (EPI == EPI_FWD) {
+        if (ea.bias != nullptr) {
+          for (int c = lane; c < BN; c += 32)
+            sb[c] = (col_base + c < ea.N) ? bias_value<KIND>(ea.bias, col_base + c) : 0.0f;
+          __syncwarp();
+        }
+      }
       if (!mbar_wait(&tfull[acc], acc_par, kStatusTimeoutAcc)) break;
       fence_after();
-      const int m_blk = tile / num_n, n_blk = tile - (tile / num_n) * num_n;
-      const int row = m_blk * BM + q * 32 + lane;
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        const int col0 = n_blk * BN + c;
+      for (int u = 0; u < BN / 64; ++u) {
+        const int col0 = col_base + u * 64;
         if (col0 >= ea.N) break;   // warp-uniform
-        uint32_t r[32];
-        tmem_ld32(tbase + (uint32_t)c, r);
-        if (row < ea.M) epilogue_chunk<KIND, EPI>(ea, row, col0, r, st);
+        const int nv = min(64, ea.N - col0);
+        uint32_t r[64];
+        tmem_ld32_nowait(tbase + (uint32_t)(u * 64), r);
+        tmem_ld32_nowait(tbase + (uint32_t)(u * 64 + 32), r + 32);
+        tmem_wait_ld();
+        if (u == BN / 64 - 1 || col0 + 64 >= ea.N) {
+          // every TMEM read of this accumulator is done: hand it back early
+          fence_before();
+          mbar_arrive(&tempty[acc]);
+        }
+        epi_unit<KIND, EPI>(ea, sb + u * 64, r, st, check, row_ok, nv);
+        if (ea.tma_out) {
+          if (row0 < ea.M) {
+            const int nbox = out16 ? 1 : 2;
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+              const int x = col0 + b * 32;
+              if (b >= nbox || x >= ea.N) break;
+              if (pending_store) {
+                if (lane == 0) bulk_wait_read_all();
+                __syncwarp();
+              }
+              stage_row(stage_buf, lane, r + 32 * b);
+              fence_async_smem();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmO, stage_buf, x, row0);
+                bulk_commit();
+              }
+              pending_store = true;
+            }
+          }
+        } else if (row_ok) {
+          store_unit_direct(ea, row, col0, nv, r, out16);
+        }
       }
-      fence_before();
-      mbar_arrive(&tempty[acc]);
+      if (col_base >= ea.N) {   // cannot happen for a valid tile; keep the barrier count exact
+        fence_before();
+        mbar_arrive(&tempty[acc]);
+      }
     }
+    if (pending_store && lane == 0) bulk_wait_all();
+    __syncwarp();
     // per-warp telemetry commit
     if constexpr (EPI == EPI_WGRAD) {
       uint32_t nz = st.nz, uf = st.uf;
@@ -444,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else {
       const uint32_t m = warp_max_u32(st.mag);
-      if (lane == 0) telem_commit(ea.amax, ea.flag, m);
+      if (lane == 0 && m != 0u) telem_commit(ea.amax, ea.flag, final_mag<KIND, EPI>(m));
     }
     if constexpr (EPI == EPI_WGRAD) {
       // named barrier over the 4 epilogue warps, then one ticket per CTA
@@ -519,6 +675,29 @@ int make_map(CUtensorMap* tm, int kind, const void* ptr, int64_t rows, int64_t K
   return r == CUDA_SUCCESS ? APA_OK : APA_ERR_CUDA;
 }
 
+// Output map for the epilogue's TMA stores: dims {N (inner), M}, row pitch
+// ldo elements, box {128 bytes, 32 rows}, 128-byte swizzle (the staging
+// layout). Returns false when the output cannot be stored this way.
+bool make_out_map(CUtensorMap* tm, const EpiArgs& ea) {
+  EncodeFn enc = get_encode();
+  if (!enc || ea.accumulate) return false;
+  int es;
+  CUtensorMapDataType dt;
+  switch (ea.out_dt) {
+    case APA_DT_F32: es = 4; dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT32; break;
+    case APA_DT_F16: es = 2; dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; break;
+    case APA_DT_BF16: es = 2; dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16; break;
+    default: return false;
+  }
+  if ((reinterpret_cast<uintptr_t>(ea.out) & 15u) != 0 || ((ea.ldo * es) & 15) != 0) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)ea.N, (cuuint64_t)ea.M};
+  cuuint64_t strides[1] = {(cuuint64_t)(ea.ldo * es)};
+  cuuint32_t box[2] = {(cuuint32_t)(128 / es), 32u};
+  cuuint32_t estr[2] = {1, 1};
+  return enc(tm, dt, 2, ea.out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+             CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <int KIND, int BN, int EPI>
 int launch_t(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea, int grid_cap, cudaStream_t s) {
   using C = Cfg<BN>;
@@ -534,10 +713,12 @@ int launch_t(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea,
   if (st) return st;
   st = make_map(&tb, KIND, B, ea.N, ea.K, ldb, BN);
   if (st) return st;
+  CUtensorMap to = ta;
+  ea.tma_out = make_out_map(&to, ea) ? 1 : 0;
   const int tiles = ((ea.M + BM - 1) / BM) * ((ea.N + BN - 1) / BN);
   int grid = std::min(tiles, grid_cap > 0 ? grid_cap : num_sms());
   if (grid < 1) grid = 1;
-  gemm_kernel<KIND, BN, EPI><<<grid, kThreads, C::kSmemBytes, s>>>(ta, tb, ea);
+  gemm_kernel<KIND, BN, EPI><<<grid, kThreads, C::kSmemBytes, s>>>(ta, tb, to, ea);
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }
 
@@ -594,7 +775,7 @@ int check_dims(int64_t M, int64_t N, int64_t K) {
 
 EpiArgs blank(int64_t M, int64_t N, int64_t K) {
   EpiArgs ea;
-  ea.out = nullptr; ea.ldo = 0; ea.out_dt = APA_DT_F32; ea.vec_out = 0;
+  ea.out = nullptr; ea.ldo = 0; ea.out_dt = APA_DT_F32; ea.vec_out = 0; ea.tma_out = 0;
   ea.bias = nullptr; ea.amax = nullptr; ea.flag = nullptr;
   ea.counters = nullptr; ea.ratio_max = nullptr; ea.vmin = 0.0f; ea.accumulate = 0;
   ea.M = (int)M; ea.N = (int)N; ea.K = (int)K;
