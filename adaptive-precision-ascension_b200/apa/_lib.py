@@ -42,7 +42,7 @@ SIGNATURES = {
     "apa_bias_grad_noalloc": [_VP, _I, _I64, _I64, _I64, _I, _VP, _I, _VP],
     "apa_ladder_pack": [_I, _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP],
     "apa_ladder_eval": [_I, _VP, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _I64, _I64,
-                        ctypes.c_double, ctypes.c_double, _VP, _VP],
+                        ctypes.c_double, ctypes.c_double, _VP, _VP, _VP],
 }
 
 _lib = None
@@ -89,7 +89,20 @@ def ptr(t) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_handle(device=None) -> int:
+    """Raw cudaStream_t of the current stream of ``device`` (the one torch
+    launches on), as an int for the C ABI."""
+    if _raw_stream is not None:
+        if device is None:
+            idx = torch.cuda.current_device()
+        elif isinstance(device, int):
+            idx = device
+        else:
+            idx = device.index if device.index is not None else torch.cuda.current_device()
+        return _raw_stream(idx)
     return torch.cuda.current_stream(device).cuda_stream
 
 

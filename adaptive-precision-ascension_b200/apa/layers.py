@@ -41,8 +41,13 @@ from .telemetry import track_telemetry_on_tensor, update_running_underflow
 _ROLES = ("input_activation", "weight", "output", "grad_output", "grad_weight", "grad_input")
 
 
+_ELEM_SIZE = {torch.float32: 4, torch.float16: 2, torch.bfloat16: 2}
+if DTYPE_MAP[LEVEL_FP8] is not None:
+    _ELEM_SIZE[DTYPE_MAP[LEVEL_FP8]] = 1
+
+
 def _elem_size(dtype: torch.dtype) -> int:
-    return torch.empty((), dtype=dtype).element_size()
+    return _ELEM_SIZE[dtype]
 
 
 def _pad(n: int, es: int) -> int:
@@ -71,8 +76,10 @@ def _operand_code(level: int) -> int:
 
 def _alloc_2d(rows: int, cols: int, dtype: torch.dtype, device) -> torch.Tensor:
     """[rows, cols] view of a buffer whose row pitch is padded to 16 bytes."""
-    buf = torch.empty(rows, _pad(cols, _elem_size(dtype)), dtype=dtype, device=device)
-    return buf[:, :cols]
+    ld = _pad(cols, _ELEM_SIZE[dtype])
+    if ld == cols:
+        return torch.empty(rows, cols, dtype=dtype, device=device)
+    return torch.empty(rows, ld, dtype=dtype, device=device)[:, :cols]
 
 
 def _update_forensic_role(tensor, role, f_amax, f_shape, f_stats, capture_argmax, f_argmax):

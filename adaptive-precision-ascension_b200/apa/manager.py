@@ -245,8 +245,7 @@ class APAManager:
                                        st.level.data_ptr(), st.ema.data_ptr(), st.O, st.oamax.data_ptr(),
                                        st.oflag.data_ptr(), glob, self.step_count, self.config.check_interval,
                                        float(self.config.theta_underflow), float(self.config.ema_alpha),
-                                       st.out.data_ptr(), s), "apa_ladder_eval")
-        st.out_host.copy_(st.out, non_blocking=True)
+                                       st.out.data_ptr(), st.out_host.data_ptr(), s), "apa_ladder_eval")
         torch.cuda.current_stream(self._global_nonfinite.device).synchronize()
         rec = st.parse()
         if rec["status"] & 1:

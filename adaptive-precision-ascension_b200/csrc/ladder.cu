@@ -67,9 +67,123 @@ __global__ void ladder_pack_kernel(int L, const float* const* amax, const float*
   if (tid == 0) packed[0] = any;
 }
 
-__global__ void ladder_eval_kernel(LadderArgs a) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+// Shared-memory image of the per-module state, filled by all threads so the
+// dependent global loads overlap; one thread then walks the modules in order.
+__global__ void __launch_bounds__(256) ladder_eval_kernel(LadderArgs a) {
+  extern __shared__ double sh_d[];
   const int L = a.L, O = a.O;
+  double* s_ema = sh_d;                                        // [L]
+  double* s_trig = s_ema + L;                                  // [L]
+  double* s_otrig = s_trig + L;                                // [O]
+  float* s_amax = reinterpret_cast<float*>(s_otrig + O);       // [L]
+  float* s_ratio = s_amax + L;                                 // [L]
+  float* s_oamax = s_ratio + L;                                // [O]
+  int* s_flag = reinterpret_cast<int*>(s_oamax + O);           // [L]
+  int* s_level = s_flag + L;                                   // [L]
+  int* s_code = s_level + L;                                   // [L]
+  int* s_oflag = s_code + L;                                   // [O]
+  int* s_ocode = s_oflag + O;                                  // [O]
+  __shared__ int s_hdr[2];
+  const int tid = threadIdx.x;
+
+  for (int i = tid; i < L; i += blockDim.x) {
+    if (a.global) {
+      s_flag[i] = a.global[1 + i] > 0;
+      s_amax[i] = __int_as_float(a.global[1 + L + i]);
+      s_ratio[i] = __int_as_float(a.global[1 + 2 * L + i]);
+    } else {
+      s_flag[i] = *a.flag[i] > 0;
+      s_amax[i] = *a.amax[i];
+      s_ratio[i] = *a.ratio[i];
+    }
+    s_level[i] = a.level[i];
+    s_ema[i] = a.ema[i];
+    s_code[i] = 0;
+    s_trig[i] = 0.0;
+  }
+  for (int j = tid; j < O; j += blockDim.x) {
+    if (a.global) {
+      s_oflag[j] = a.global[1 + 3 * L + j] > 0;
+      s_oamax[j] = __int_as_float(a.global[1 + 3 * L + O + j]);
+    } else {
+      s_oflag[j] = *a.oflag[j] > 0;
+      s_oamax[j] = *a.oamax[j];
+    }
+    s_ocode[j] = 0;
+    s_otrig[j] = 0.0;
+  }
+  __syncthreads();
+
+  if (tid == 0) {
+    bool hard = false;
+    if (a.global) {
+      hard = a.global[0] > 0;
+    } else {
+      for (int i = 0; i < L && !hard; ++i) hard = s_flag[i];
+      for (int j = 0; j < O && !hard; ++j) hard = s_oflag[j];
+    }
+    const bool eval = hard || (a.interval > 0 && (a.step % a.interval) == 0);
+    int status = 0;
+    int min_level = 1;
+    if (eval) {
+      status |= 1;
+      bool overflow = false;
+      for (int i = 0; i < L; ++i) {
+        const double av = (double)s_amax[i];
+        const bool nonf = s_flag[i] != 0;
+        const int old = s_level[i];
+        const double thr = thr_of(a, old);
+        int reason = 0;
+        double t = 0.0;
+        if (nonf || isinf(av) || isnan(av) || av > thr) {
+          overflow = true;
+          reason = 1;
+          t = (nonf && !isinf(av) && !isnan(av) && av <= thr) ? (double)NAN : av;
+        } else {
+          const double r = (double)s_ratio[i];
+          // alpha * ema + (1 - alpha) * r, each operation rounded as Python does
+          const double e = __dadd_rn(__dmul_rn(a.alpha, s_ema[i]), __dmul_rn(__dsub_rn(1.0, a.alpha), r));
+          s_ema[i] = e;
+          if (e > a.theta) {
+            reason = 2;
+            t = e;
+          }
+        }
+        int c = 0;
+        if (reason) {
+          c = reason | (old << 4);
+          if (old < 2) {
+            s_level[i] = old + 1;
+            s_ema[i] = 0.0;
+            c |= 4;
+            status |= 4;
+          }
+        }
+        s_code[i] = c;
+        s_trig[i] = t;
+      }
+      if (L > 0) {
+        min_level = s_level[0];
+        for (int i = 1; i < L; ++i) min_level = min(min_level, s_level[i]);
+      }
+      const double othr = thr_of(a, min_level);
+      for (int j = 0; j < O; ++j) {
+        const double av = (double)s_oamax[j];
+        const bool nonf = s_oflag[j] != 0;
+        if (nonf || isinf(av) || isnan(av) || av > othr) {
+          overflow = true;
+          s_ocode[j] = 1;
+          s_otrig[j] = (nonf && !isinf(av) && !isnan(av)) ? (double)NAN : av;
+        }
+      }
+      if (overflow) status |= 2;
+    }
+    s_hdr[0] = status;
+    s_hdr[1] = min_level;
+  }
+  __syncthreads();
+
+  const int status = s_hdr[0];
   int* hdr = reinterpret_cast<int*>(a.out);
   int* code = hdr + 4;
   int* ocode = code + L;
@@ -79,92 +193,43 @@ __global__ void ladder_eval_kernel(LadderArgs a) {
   double* ema_out = dbl;
   double* trig = dbl + L;
   double* otrig = trig + L;
-
-  auto flag_of = [&](int i) -> bool { return a.global ? a.global[1 + i] > 0 : *a.flag[i] > 0; };
-  auto amax_of = [&](int i) -> float { return a.global ? __int_as_float(a.global[1 + L + i]) : *a.amax[i]; };
-  auto ratio_of = [&](int i) -> float { return a.global ? __int_as_float(a.global[1 + 2 * L + i]) : *a.ratio[i]; };
-  auto oflag_of = [&](int j) -> bool { return a.global ? a.global[1 + 3 * L + j] > 0 : *a.oflag[j] > 0; };
-  auto oamax_of = [&](int j) -> float { return a.global ? __int_as_float(a.global[1 + 3 * L + O + j]) : *a.oamax[j]; };
-
-  bool hard = false;
-  if (a.global) {
-    hard = a.global[0] > 0;
-  } else {
-    for (int i = 0; i < L && !hard; ++i) hard = flag_of(i);
-    for (int j = 0; j < O && !hard; ++j) hard = oflag_of(j);
-  }
-  const bool eval = hard || (a.interval > 0 && (a.step % a.interval) == 0);
-  int status = 0;
-  int min_level = 1;
-  for (int i = 0; i < L; ++i) { code[i] = 0; trig[i] = 0.0; }
-  for (int j = 0; j < O; ++j) { ocode[j] = 0; otrig[j] = 0.0; }
-  if (eval) {
-    status |= 1;
-    bool overflow = false;
-    for (int i = 0; i < L; ++i) {
-      const double av = (double)amax_of(i);
-      const bool nonf = flag_of(i);
-      const int old = a.level[i];
-      const double thr = thr_of(a, old);
-      int reason = 0;
-      double t = 0.0;
-      if (nonf || isinf(av) || isnan(av) || av > thr) {
-        overflow = true;
-        reason = 1;
-        t = (nonf && !isinf(av) && !isnan(av) && av <= thr) ? (double)NAN : av;
-      } else {
-        const double r = (double)ratio_of(i);
-        // alpha * ema + (1 - alpha) * r, each operation rounded as Python does
-        const double e = __dadd_rn(__dmul_rn(a.alpha, a.ema[i]), __dmul_rn(__dsub_rn(1.0, a.alpha), r));
-        a.ema[i] = e;
-        if (e > a.theta) {
-          reason = 2;
-          t = e;
-        }
-      }
-      int c = 0;
-      if (reason) {
-        c = reason | (old << 4);
-        if (old < 2) {
-          a.level[i] = old + 1;
-          a.ema[i] = 0.0;
-          c |= 4;
-          status |= 4;
-        }
-      }
-      code[i] = c;
-      trig[i] = t;
+  for (int i = tid; i < L; i += blockDim.x) {
+    a.level[i] = s_level[i];
+    a.ema[i] = s_ema[i];
+    lvl_out[i] = s_level[i];
+    ema_out[i] = s_ema[i];
+    code[i] = s_code[i];
+    trig[i] = s_trig[i];
+    if (status & 1) {
       // reset the window (manager.py:237-239); the pointers are the module's own buffers
       *a.amax[i] = 0.0f;
       *a.ratio[i] = 0.0f;
       *a.flag[i] = 0;
     }
-    if (L > 0) {
-      min_level = a.level[0];
-      for (int i = 1; i < L; ++i) min_level = min(min_level, a.level[i]);
-    }
-    const double othr = thr_of(a, min_level);
-    for (int j = 0; j < O; ++j) {
-      const double av = (double)oamax_of(j);
-      const bool nonf = oflag_of(j);
-      if (nonf || isinf(av) || isnan(av) || av > othr) {
-        overflow = true;
-        ocode[j] = 1;
-        otrig[j] = (nonf && !isinf(av) && !isnan(av)) ? (double)NAN : av;
-      }
+  }
+  for (int j = tid; j < O; j += blockDim.x) {
+    ocode[j] = s_ocode[j];
+    otrig[j] = s_otrig[j];
+    if (status & 1) {
       *a.oamax[j] = 0.0f;
       *a.oflag[j] = 0;
     }
-    if (overflow) status |= 2;
   }
-  for (int i = 0; i < L; ++i) {
-    lvl_out[i] = a.level[i];
-    ema_out[i] = a.ema[i];
+  if (tid == 0) {
+    hdr[0] = status;
+    hdr[1] = s_hdr[1];
+    hdr[2] = L;
+    hdr[3] = O;
   }
-  hdr[0] = status;
-  hdr[1] = min_level;
-  hdr[2] = L;
-  hdr[3] = O;
+}
+
+size_t ladder_smem_bytes(int L, int O) {
+  return (size_t)(2 * L + O) * sizeof(double) + (size_t)(2 * L + O) * sizeof(float) + (size_t)(3 * L + 2 * O) * sizeof(int);
+}
+
+size_t ladder_record_bytes(int L, int O) {
+  const size_t nint = 4 + 2 * (size_t)L + O;
+  return ((nint * 4 + 7) & ~(size_t)7) + 8 * (2 * (size_t)L + O);
 }
 
 }  // namespace
@@ -202,7 +267,8 @@ extern "C" int apa_ladder_pack(int L, const float* const* amax_ptr, const float*
 extern "C" int apa_ladder_eval(int L, float* const* amax_ptr, float* const* ratio_ptr, int32_t* const* flag_ptr,
                                int32_t* level, double* ema, int O, float* const* oamax_ptr,
                                int32_t* const* oflag_ptr, const int32_t* global, int64_t step_count,
-                               int64_t check_interval, double theta, double alpha, void* out, void* stream) {
+                               int64_t check_interval, double theta, double alpha, void* out, void* out_host,
+                               void* stream) {
   if (L < 0 || O < 0 || !out) return APA_ERR_INVALID;
   if ((L > 0 && (!amax_ptr || !ratio_ptr || !flag_ptr || !level || !ema)) || (O > 0 && (!oamax_ptr || !oflag_ptr)))
     return APA_ERR_INVALID;
@@ -219,6 +285,17 @@ extern "C" int apa_ladder_eval(int L, float* const* amax_ptr, float* const* rati
   a.thr1 = 0.90 * 65504.0;
   a.thr2 = (double)INFINITY;
   a.out = static_cast<char*>(out);
-  ladder_eval_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  const size_t smem = ladder_smem_bytes(L, O);
+  if (smem > 200 * 1024) return APA_ERR_INVALID;   // far beyond any model's module count
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (smem > 48 * 1024) {
+    if (cudaFuncSetAttribute(ladder_eval_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return APA_ERR_CUDA;
+  }
+  ladder_eval_kernel<<<1, 256, smem, st>>>(a);
+  if (cudaGetLastError() != cudaSuccess) return APA_ERR_CUDA;
+  if (out_host != nullptr &&
+      cudaMemcpyAsync(out_host, out, ladder_record_bytes(L, O), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return APA_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }

@@ -198,8 +198,10 @@ int apa_bias_grad_noalloc(const void* dy, int dy_dtype, int64_t rows, int64_t co
  * `global` (nullable, int32[1 + 3L + 2O]): when given, the telemetry is read
  * from this already-reduced vector (see apa_ladder_pack) instead of the
  * pointers, so every data-parallel rank decides identically.
- * `out` (int32[4 + 2L + O] + double[2L + O] as described in apa_ladder.cu) receives
- * the decision record the host uses for logging.
+ * `out` (device memory; int32[4 + 2L + O], padded to 8 bytes, then
+ * double[2L + O]) receives the decision record the host uses for logging;
+ * when `out_host` (pinned host memory) is given the record is also copied there
+ * on the same stream, so the host needs one stream synchronisation.
  */
 int apa_ladder_pack(int L, const float* const* amax_ptr, const float* const* ratio_ptr,
                     const int32_t* const* flag_ptr, int O, const float* const* oamax_ptr,
@@ -208,7 +210,7 @@ int apa_ladder_pack(int L, const float* const* amax_ptr, const float* const* rat
 int apa_ladder_eval(int L, float* const* amax_ptr, float* const* ratio_ptr, int32_t* const* flag_ptr,
                     int32_t* level, double* ema, int O, float* const* oamax_ptr, int32_t* const* oflag_ptr,
                     const int32_t* global, int64_t step_count, int64_t check_interval, double theta,
-                    double alpha, void* out, void* stream);
+                    double alpha, void* out, void* out_host, void* stream);
 
 #ifdef __cplusplus
 }

@@ -47,6 +47,6 @@ def test_invalid_arguments_rejected_without_gpu():
     assert lib.apa_linear_dgrad(0, 16, 16, 16, 16, 16, 9, 16, 16, 16, 16, None, None, None) == _lib.ERR_UNSUPPORTED
     assert lib.apa_linear_wgrad(0, 16, 16, 16, 16, 16, 16, 16, 16, 16, 0, None, None, None) == _lib.ERR_INVALID
     assert lib.apa_ladder_eval(-1, None, None, None, None, None, 0, None, None, None, 1, 1, 0.4, 0.95, None,
-                               None) == _lib.ERR_INVALID
+                               None, None) == _lib.ERR_INVALID
     assert lib.apa_amax(None, 0, 5, None, None, None) == _lib.ERR_INVALID
     assert lib.apa_zero_list(None, 3, None) == _lib.ERR_INVALID

@@ -1,0 +1,116 @@
+"""Data-parallel host logic on CPU with two gloo ranks (no GPU):
+
+* GradientAverager: gradients written into the flat buckets by autograd are
+  averaged across ranks, buckets are issued in a fixed order as they fill, and
+  zero_grad(set_to_none=True) between steps is handled by re-arming.
+* The ladder's telemetry reduction: amax / ratio encoded as int32 bit
+  patterns reduce under MAX to the float maximum, with NaN dominating, so every
+  rank evaluates the same global values (the reference evaluates local values
+  only, manager.py:221-256).
+"""
+import math
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+import torch.nn as nn
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+class _FakeManager:
+    """The two things GradientAverager reads from APAManager."""
+
+    def __init__(self, model):
+        self.model = model
+        self.apa_modules = {}
+
+    def get_trainable_parameters(self):
+        return [p for p in self.model.parameters() if p.requires_grad]
+
+
+def _averager_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from apa.dp import GradientAverager
+        torch.manual_seed(0)                       # identical weights on both ranks
+        model = nn.Sequential(nn.Linear(6, 5), nn.ReLU(), nn.Linear(5, 3), nn.LayerNorm(3))
+        avg = GradientAverager(_FakeManager(model), None, bucket_bytes=64)   # several small buckets
+        results = []
+        for step in range(3):
+            avg.arm()
+            g = torch.Generator().manual_seed(100 * step + rank)          # different data per rank
+            x = torch.randn(4, 6, generator=g)
+            model(x).pow(2).sum().backward()
+            local = [p.grad.clone() for p in model.parameters()]
+            issued_before_finish = avg.next
+            avg.finish()
+            results.append(([p.grad.tolist() for p in model.parameters()], [t.tolist() for t in local],
+                            issued_before_finish, len(avg.buckets)))
+            for p in model.parameters():
+                p.grad = None                      # zero_grad(set_to_none=True)
+        q.put((rank, results))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gradient_averager_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_averager_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for step in range(3):
+        avg0, local0, issued0, nb = out[0][step]
+        avg1, local1, issued1, _ = out[1][step]
+        assert nb > 1
+        assert issued0 == issued1 == nb            # every bucket issued by the hooks, in order
+        for a0, a1, l0, l1 in zip(avg0, avg1, local0, local1):
+            a0, a1, l0, l1 = (torch.tensor(v) for v in (a0, a1, l0, l1))
+            want = (l0 + l1) / 2
+            assert torch.allclose(a0, want, atol=1e-6) and torch.equal(a0, a1)
+
+
+def _telemetry_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        vals = {0: [0.5, 3.0, 0.0, float("inf"), 1.0], 1: [2.0, float("nan"), 0.25, 7.0, 0.0]}[rank]
+        t = torch.tensor(vals, dtype=torch.float32).view(torch.int32).clone()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        q.put((rank, t.view(torch.float32).tolist()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_telemetry_bit_pattern_max_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_telemetry_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in (0, 1):
+        v = out[r]
+        assert v[0] == 2.0 and math.isnan(v[1]) and v[2] == 0.25 and math.isinf(v[3]) and v[4] == 1.0
