@@ -33,6 +33,12 @@ class _Bucket:
         self.handle = None
 
 
+# SMs left to the collective's kernel while a bucket all-reduce is in flight:
+# the persistent GEMMs otherwise occupy every SM and the all-reduce could only
+# start after them.
+RESERVED_SMS = 16
+
+
 class GradientAverager:
     def __init__(self, mgr, process_group=None, bucket_bytes: int = 64 << 20):
         self.pg = process_group
@@ -57,6 +63,7 @@ class GradientAverager:
                 self.where[id(p)] = bi
         self.next = 0
         self.armed = False
+        self.limited = False
         apa_params = set()
         for m in mgr.apa_modules.values():
             m._grad_ready_cb = self._apa_ready
@@ -98,7 +105,19 @@ class GradientAverager:
     def _param_ready(self, p):
         self._mark(p)
 
+    def _limit_gemms(self, on: bool):
+        if self.buckets and self.buckets[0].flat.is_cuda:
+            from . import _lib
+            n = 0
+            if on:
+                n = max(1, torch.cuda.get_device_properties(self.buckets[0].flat.device).multi_processor_count
+                        - RESERVED_SMS)
+            _lib.check(_lib.lib().apa_set_gemm_sm_limit(n), "apa_set_gemm_sm_limit")
+
     def _launch(self, b: _Bucket):
+        if not self.limited:
+            self._limit_gemms(True)
+            self.limited = True
         if self.avg_op is not None:
             b.handle = dist.all_reduce(b.flat, op=self.avg_op, group=self.pg, async_op=True)
         else:
@@ -131,4 +150,7 @@ class GradientAverager:
                     else:
                         dist.all_reduce(p.grad, op=dist.ReduceOp.SUM, group=self.pg)
                         p.grad.div_(self.world)
+        if self.limited:
+            self._limit_gemms(False)
+            self.limited = False
         self.armed = False

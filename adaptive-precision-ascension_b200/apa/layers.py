@@ -248,20 +248,8 @@ class _APALinearFn(torch.autograd.Function):
 
         first = mod._grad_epoch != mod._epoch
         mod._grad_epoch = mod._epoch
-        dx = None
-        if need_dx:
-            wqt = ctx.wqt
-            if wqt is None or mod._wqt_stale:
-                mod._make_wqt()
-                wqt = mod._wqt
-            dx = torch.empty(M, K, dtype=ctx.xdtype, device=dev)
-            bc = mod.boundary_cast
-            st = lib.apa_linear_dgrad(level, dyq.data_ptr(), dyq.stride(0), wqt.data_ptr(), wqt.stride(0),
-                                      dx.data_ptr(), _lib.dt_code(ctx.xdtype), K, M, N, K,
-                                      _lib.ptr(getattr(bc, "gpu_amax", None)),
-                                      _lib.ptr(getattr(bc, "gpu_has_nonfinite", None)), s)
-            _lib.check(st, "apa_linear_dgrad")
-            dx = dx.view(*ctx.lead, K)
+        # weight and bias gradients first: in data-parallel runs their bucket
+        # all-reduce then overlaps the input-gradient GEMM below
         if need_dw:
             W = mod.weight_master
             g = W.grad
@@ -291,13 +279,27 @@ class _APALinearFn(torch.autograd.Function):
             _lib.check(st, "apa_colsum_finalize")
             if b.grad is None:
                 b.grad = g
+        if need_dw:
+            mod._notify_grad_ready()
+        dx = None
+        if need_dx:
+            wqt = ctx.wqt
+            if wqt is None or mod._wqt_stale:
+                mod._make_wqt()
+                wqt = mod._wqt
+            dx = torch.empty(M, K, dtype=ctx.xdtype, device=dev)
+            bc = mod.boundary_cast
+            st = lib.apa_linear_dgrad(level, dyq.data_ptr(), dyq.stride(0), wqt.data_ptr(), wqt.stride(0),
+                                      dx.data_ptr(), _lib.dt_code(ctx.xdtype), K, M, N, K,
+                                      _lib.ptr(getattr(bc, "gpu_amax", None)),
+                                      _lib.ptr(getattr(bc, "gpu_has_nonfinite", None)), s)
+            _lib.check(st, "apa_linear_dgrad")
+            dx = dx.view(*ctx.lead, K)
         if f_on and dx is not None:
             _update_forensic_role(dx, "grad_input", *mod._forensic_args())
         mod._needs_wt = need_dx
         ctx.xqt = None
         ctx.wqt = None
-        if need_dw:
-            mod._notify_grad_ready()
         return dx, None, None, None
 
 

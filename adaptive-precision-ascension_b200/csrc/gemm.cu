@@ -731,6 +731,10 @@ int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea
 
 }  // namespace gemm
 
+// Upper bound on the persistent grid (0 = one CTA per SM). Set while a
+// collective runs concurrently, so its kernel finds free SMs.
+static int g_gemm_sm_limit = 0;
+
 // Choose the N tile: 256 keeps shared-memory traffic per MMA lowest; 128 when
 // N is small or 256-wide tiles would leave SMs idle.
 int pick_bn(int64_t M, int64_t N) {
@@ -745,6 +749,7 @@ int gemm_dispatch(int rung, int epi, const void* A, int64_t lda, const void* B, 
                   int bn, int grid_cap, cudaStream_t s) {
   using namespace gemm;
   if (bn != 128 && bn != 256) bn = pick_bn(ea.M, ea.N);
+  if (grid_cap <= 0 && g_gemm_sm_limit > 0) grid_cap = g_gemm_sm_limit;
 #define APA_EPI_CASE(KIND)                                                               \
   switch (epi) {                                                                          \
     case EPI_FWD: return launch_bn<KIND, EPI_FWD>(A, lda, B, ldb, ea, bn, grid_cap, s);   \
@@ -830,6 +835,12 @@ extern "C" int apa_linear_wgrad(int rung, const void* dyqt, int64_t lddyt, const
   ea.vmin = rung == APA_RUNG_FP8 ? 0.015625f : rung == APA_RUNG_FP16 ? 6.1035e-5f : 0.0f;
   return apa::gemm_dispatch(rung, apa::gemm::EPI_WGRAD, dyqt, lddyt, xqt, ldxt, ea, 0, 0,
                             static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int apa_set_gemm_sm_limit(int limit) {
+  if (limit < 0) return APA_ERR_INVALID;
+  apa::g_gemm_sm_limit = limit;
+  return APA_OK;
 }
 
 extern "C" int apa_gemm_tn(int rung, int epilogue, const void* A, int64_t lda, const void* B, int64_t ldb, void* out,

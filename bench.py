@@ -452,7 +452,17 @@ def main():
         return
     if args.warmup < 3:
         args.warmup = 3
-    out = run_reference(args) if args.impl == "reference" else run_ours(args)
+    # libraries (NCCL, the reference's event logger) print to stdout; route the
+    # process's fd 1 to stderr while working so stdout carries one JSON line
+    sys.stdout.flush()
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        out = run_reference(args) if args.impl == "reference" else run_ours(args)
+    finally:
+        sys.stdout.flush()
+        os.dup2(json_fd, 1)
+        os.close(json_fd)
     if out is not None:
         print(json.dumps(out), flush=True)
 

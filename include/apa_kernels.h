@@ -157,6 +157,14 @@ int apa_linear_wgrad(int rung, const void* dyqt, int64_t lddyt, const void* xqt,
                      unsigned long long* counters, float* ratio_max, void* stream);
 
 /*
+ * Cap the number of CTAs (SMs) the persistent GEMMs use; 0 restores one CTA
+ * per SM. Process-wide. The data-parallel path sets it while a gradient
+ * all-reduce runs alongside a GEMM so the collective's kernel finds free SMs.
+ * No counterpart in the reference (it has no gradient collective).
+ */
+int apa_set_gemm_sm_limit(int limit);
+
+/*
  * The same tcgen05 GEMM with a chosen epilogue and no telemetry side effects,
  * optional N tile (128/256, 0 = automatic) and grid cap (0 = one CTA per SM).
  * Used to time the bare GEMM against the fused entry points.

@@ -44,16 +44,22 @@ def _averager_worker(rank, world, port, q):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         from apa.dp import GradientAverager
-        torch.manual_seed(0)                       # identical weights on both ranks
-        model = nn.Sequential(nn.Linear(6, 5), nn.ReLU(), nn.Linear(5, 3), nn.LayerNorm(3))
+        def build():
+            torch.manual_seed(0)                   # identical weights on both ranks
+            return nn.Sequential(nn.Linear(6, 5), nn.ReLU(), nn.Linear(5, 3), nn.LayerNorm(3))
+
+        model, plain = build(), build()            # plain: same model without the averager
         avg = GradientAverager(_FakeManager(model), None, bucket_bytes=64)   # several small buckets
         results = []
         for step in range(3):
-            avg.arm()
             g = torch.Generator().manual_seed(100 * step + rank)          # different data per rank
             x = torch.randn(4, 6, generator=g)
+            plain(x).pow(2).sum().backward()
+            local = [p.grad.clone() for p in plain.parameters()]
+            for p in plain.parameters():
+                p.grad = None
+            avg.arm()
             model(x).pow(2).sum().backward()
-            local = [p.grad.clone() for p in model.parameters()]
             issued_before_finish = avg.next
             avg.finish()
             results.append(([p.grad.tolist() for p in model.parameters()], [t.tolist() for t in local],
