@@ -64,6 +64,7 @@ class GradientAverager:
         self.next = 0
         self.armed = False
         self.limited = False
+        self.graphed = False
         apa_params = set()
         for m in mgr.apa_modules.values():
             m._grad_ready_cb = self._apa_ready
@@ -128,9 +129,20 @@ class GradientAverager:
             self._launch(self.buckets[self.next])
             self.next += 1
 
+    def graph_captured(self):
+        """The step was captured into a CUDA graph: its bucket all-reduces are
+        part of the graph and run on every replay, so finish() has nothing
+        left to issue or wait for."""
+        self.graphed = True
+        if self.limited:
+            self._limit_gemms(False)
+            self.limited = False
+
     def finish(self):
         """Issue every bucket not yet issued (in order) and make the current
         stream wait for all of them; average when the backend has no AVG."""
+        if self.graphed:
+            return
         while self.next < len(self.buckets):
             self._launch(self.buckets[self.next])
             self.next += 1

@@ -409,6 +409,22 @@ __device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const uint32_t
         make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
 }
 
+// Tile order: groups of kGroupM consecutive M blocks, N advancing across a
+// group and M fastest inside it, so the CTAs running at the same time share
+// their B tiles (and a group's A rows) in L2 even when B is larger than L2
+// (e.g. a 50k-row vocabulary projection).
+constexpr int kGroupM = 16;
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& m_blk, int& n_blk) {
+  const int group_tiles = kGroupM * num_n;
+  const int g = tile / group_tiles;
+  const int first_m = g * kGroupM;
+  const int gs = min(kGroupM, num_m - first_m);
+  const int local = tile - g * group_tiles;
+  m_blk = first_m + local % gs;
+  n_blk = local / gs;
+}
+
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
@@ -434,7 +450,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_n = (ea.N + BN - 1) / BN;
-  const int num_tiles = ((ea.M + BM - 1) / BM) * num_n;
+  const int num_m = (ea.M + BM - 1) / BM;
+  const int num_tiles = num_m * num_n;
   const int kb_count = (int)(((int64_t)ea.K * KindInfo<KIND>::bytes + kSlab - 1) / kSlab);
 
   if (threadIdx.x == 0) {
@@ -465,7 +482,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        const int m_blk = tile / num_n, n_blk = tile - (tile / num_n) * num_n;
+        int m_blk, n_blk;
+        tile_coords(tile, num_m, num_n, m_blk, n_blk);
         for (int kb = 0; kb < kb_count; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, kStatusTimeoutEmpty)) { ok = false; break; }
           mbar_expect_tx(&full[stage], C::kStageBytes);
@@ -523,7 +541,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
-      const int m_blk = tile / num_n, n_blk = tile - (tile / num_n) * num_n;
+      int m_blk, n_blk;
+      tile_coords(tile, num_m, num_n, m_blk, n_blk);
       const int col_base = n_blk * BN;
       const int row0 = m_blk * BM + q * 32;
       const int row = row0 + lane;

@@ -197,6 +197,12 @@ def run_ours(args):
 
     # end to end: host-resident inputs, copied in every step, result read back
     e2e = run_e2e(torch, make, x, dy32, dev, args, world, barrier, max_over_ranks)
+    del x, dy32, dy16
+    torch.cuda.empty_cache()
+    gpt = {}
+    for name in args.gpt:
+        gpt[name] = run_gpt(torch, dist, name, world, rank, dev, args.gpt_steps, max(4, args.warmup), barrier,
+                            max_over_ranks, graphed=not args.gpt_eager)
     out = None
     if rank == 0:
         fp8 = results["fp8"]
@@ -209,6 +215,7 @@ def run_ours(args):
                           "frac_of_peak": round(v["frac_of_peak"], 4)} for k, v in results.items()},
             "roofline": gemm_roof,
             "e2e": e2e,
+            "gpt": gpt,
             "gpu_launches": launches,
             "clocks": clocks,
             "peaks": pk,
@@ -217,6 +224,185 @@ def run_ours(args):
             out["cpu_baseline"] = cpu_baseline(args, sample_steps=1)
     if world > 1:
         dist.destroy_process_group()
+    return out
+
+
+
+# ---------------------------------------------------------------------------
+# GPT training workloads (harness: the model around the APALinear layers)
+# ---------------------------------------------------------------------------
+GPT_CONFIGS = {
+    # char-level nanoGPT: 6 layers, 6 heads, d 384, context 256, vocab 65,
+    # per-GPU batch 64, uniform tokens, AdamW 1e-3, default config
+    "gpt-char": dict(n_layer=6, n_head=6, d=384, T=256, vocab=65, vocab_pad=65, batch=64, lr=1e-3,
+                     zipf=None, preset="default", preset_levels=False),
+    # GPT-2-medium shape: 24 layers, 16 heads, d 1024, context 1024, vocab
+    # 50257, per-GPU batch 8, Zipf(1.1) tokens, aggressive() config, QKV of
+    # layers 0-3 at FP16 and the LM head at TF32 from the start. The LM head
+    # has 50304 outputs (16-byte aligned rows); the 47 extra classes carry a
+    # -30000 bias in fp32 (the head starts at TF32 and the ladder only moves
+    # up), so their softmax probability and gradients are exactly zero and the
+    # model computes the 50257-class function without slicing the logits.
+    "gpt2m": dict(n_layer=24, n_head=16, d=1024, T=1024, vocab=50257, vocab_pad=50304, batch=8, lr=1e-4,
+                  zipf=1.1, preset="aggressive", preset_levels=True),
+}
+
+
+def build_gpt(torch, nn, F, apa, cfgd, device):
+    from apa import APAConfig, APALinear
+    preset = {"default": APAConfig, "aggressive": APAConfig.aggressive}[cfgd["preset"]]
+    cfg = preset(device=str(device)) if cfgd["preset"] != "default" else APAConfig(device=str(device))
+    d, H, T = cfgd["d"], cfgd["n_head"], cfgd["T"]
+
+    class LayerNorm32(nn.LayerNorm):
+        """LayerNorm in fp32 that accepts the fp16 outputs of FP16-rung layers
+        and returns fp32 (the residual stream's dtype)."""
+
+        def forward(self, x):
+            return F.layer_norm(x.float(), self.normalized_shape, self.weight, self.bias, self.eps)
+
+    class Attention(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.c_attn = APALinear(d, 3 * d, config=cfg)
+            self.c_proj = APALinear(d, d, config=cfg)
+
+        def forward(self, x):
+            B, Tq, C = x.shape
+            q, k, v = self.c_attn(x).to(torch.bfloat16).split(C, dim=2)
+            q = q.view(B, Tq, H, C // H).transpose(1, 2)
+            k = k.view(B, Tq, H, C // H).transpose(1, 2)
+            v = v.view(B, Tq, H, C // H).transpose(1, 2)
+            y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+            return self.c_proj(y.transpose(1, 2).reshape(B, Tq, C))
+
+    class MLP(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.c_fc = APALinear(d, 4 * d, config=cfg)
+            self.gelu = nn.GELU()
+            self.c_proj = APALinear(4 * d, d, config=cfg)
+
+        def forward(self, x):
+            return self.c_proj(self.gelu(self.c_fc(x).float()))
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.ln_1 = LayerNorm32(d)
+            self.attn = Attention()
+            self.ln_2 = LayerNorm32(d)
+            self.mlp = MLP()
+
+        def forward(self, x):
+            x = x + self.attn(self.ln_1(x)).float()
+            return x + self.mlp(self.ln_2(x)).float()
+
+    class GPT(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.token_embedding = nn.Embedding(cfgd["vocab"], d)
+            self.position_embedding = nn.Embedding(T, d)
+            self.blocks = nn.ModuleList([Block() for _ in range(cfgd["n_layer"])])
+            self.ln_f = LayerNorm32(d)
+            self.lm_head = APALinear(d, cfgd["vocab_pad"], config=cfg)
+
+        def forward(self, idx):
+            B, Tq = idx.shape
+            pos = torch.arange(Tq, device=idx.device)
+            x = self.token_embedding(idx) + self.position_embedding(pos)
+            for blk in self.blocks:
+                x = blk(x)
+            return self.lm_head(self.ln_f(x))
+
+    torch.manual_seed(0)
+    model = GPT().to(device)
+    if cfgd["preset_levels"]:
+        for i in range(4):
+            model.blocks[i].attn.c_attn.level = 1
+        model.lm_head.level = 2
+    if cfgd["vocab_pad"] > cfgd["vocab"]:
+        assert model.lm_head.level == 2, "padded classes need an fp32 bias"
+        with torch.no_grad():
+            model.lm_head.bias_master[cfgd["vocab"]:] = -30000.0
+    return model, cfg
+
+
+def gpt_batches(torch, cfgd, rank, device, n=4):
+    g = torch.Generator().manual_seed(1234 + rank)
+    B, T, V = cfgd["batch"], cfgd["T"], cfgd["vocab"]
+    out = []
+    for _ in range(n):
+        if cfgd["zipf"]:
+            ranks = torch.arange(1, V + 1, dtype=torch.float64)
+            p = ranks.pow(-cfgd["zipf"])
+            idx = torch.multinomial(p / p.sum(), B * (T + 1), replacement=True, generator=g)
+        else:
+            idx = torch.randint(0, V, (B * (T + 1),), generator=g)
+        idx = idx.view(B, T + 1)
+        out.append((idx[:, :T].contiguous().to(device), idx[:, 1:].contiguous().to(device)))
+    return out
+
+
+def run_gpt(torch, dist, name, world, rank, dev, steps, warmup, barrier, max_over_ranks, graphed=True):
+    import torch.nn as nn
+    import torch.nn.functional as F
+    import apa
+    from apa import APAManager
+    cfgd = GPT_CONFIGS[name]
+    model, cfg = build_gpt(torch, nn, F, apa, cfgd, dev)
+    mgr = APAManager(model, cfg)
+    opt = torch.optim.AdamW(mgr.get_trainable_parameters(), lr=cfgd["lr"], weight_decay=0.01, fused=True)
+    batches = gpt_batches(torch, cfgd, rank, dev)
+    V = cfgd["vocab_pad"]
+
+    def loss_fn(x, y):
+        return F.cross_entropy(model(x).reshape(-1, V).float(), y.reshape(-1))
+
+    if graphed:
+        from apa.graphs import GraphedTrainStep
+        gstep = GraphedTrainStep(mgr, loss_fn, batches[0], warmup=2)
+
+        def step(i):
+            loss, keep = gstep(*batches[i % len(batches)])
+            if keep:
+                opt.step()
+            return loss
+    else:
+        def step(i):
+            x, y = batches[i % len(batches)]
+            mgr.pre_step()
+            opt.zero_grad(set_to_none=True)
+            loss = loss_fn(x, y)
+            loss.backward()
+            if mgr.post_backward_sync_and_eval():
+                opt.step()
+            else:
+                opt.zero_grad(set_to_none=True)
+            return loss
+
+    for i in range(warmup):
+        step(i)
+    barrier()
+    s = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(steps):
+        loss = step(warmup + i)
+    e1.record(s)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    tokens = world * cfgd["batch"] * cfgd["T"]
+    nparam = sum(m.weight_master.numel() for m in mgr.apa_modules.values())
+    levels = {}
+    for m in mgr.apa_modules.values():
+        levels[m.level] = levels.get(m.level, 0) + 1
+    out = {"tokens_per_s": round(tokens / ms * 1e3, 1), "ms_per_step": round(ms, 3), "global_batch_tokens": tokens,
+           "mode": "cuda-graph replay of pre_step+fwd+bwd" if graphed else "eager",
+           "apa_linear_params": nparam, "levels": {["fp8", "fp16", "tf32"][k]: v for k, v in sorted(levels.items())},
+           "loss": round(float(loss.item()), 4)}
+    del model, mgr, opt
+    torch.cuda.empty_cache()
     return out
 
 
@@ -444,6 +630,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gpt", default="gpt-char,gpt2m",
+                    help="GPT training workloads also timed (tokens/s), comma-separated; '' for none")
+    ap.add_argument("--gpt-steps", type=int, default=10)
+    ap.add_argument("--gpt-eager", action="store_true", help="time the GPT workloads without CUDA-graph replay")
     ap.add_argument("--profile-case", default=None,
                     help="run a few launches of one kernel for an ncu capture (gemm-fp8|gemm-fp16|gemm-tf32|cast|dyprep)")
     args = ap.parse_args()
@@ -452,6 +642,7 @@ def main():
         return
     if args.warmup < 3:
         args.warmup = 3
+    args.gpt = [g for g in args.gpt.split(",") if g]
     # libraries (NCCL, the reference's event logger) print to stdout; route the
     # process's fd 1 to stderr while working so stdout carries one JSON line
     sys.stdout.flush()
