@@ -3,5 +3,6 @@
 // than as relocatable device code.
 #include "cast.cu"
 #include "gemm.cu"
+#include "cast_tma.cu"
 #include "ladder.cu"
 #include "noalloc.cu"

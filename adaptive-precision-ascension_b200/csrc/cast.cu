@@ -511,6 +511,9 @@ int launch_cast_dst(int dst_dt, CastParams& p, cudaStream_t s) {
 
 }  // namespace
 
+// streaming TMA version for the aligned E4M3 / fp16 layouts (cast_tma.cu)
+int cast_tma_try(int src_dt, int dst_dt, const CastParams& p, cudaStream_t s);
+
 int cast_dispatch(int src_dt, int dst_dt, CastParams& p, cudaStream_t s) {
   switch (src_dt) {
     case APA_DT_F32: return launch_cast_dst<APA_DT_F32>(dst_dt, p, s);
@@ -547,6 +550,8 @@ extern "C" int apa_cast(const void* src, int src_dtype, int64_t rows, int64_t co
   p.vec_src = aligned16(src, ld_src, es_src);
   p.vec_dst = aligned16(dst, ld_dst, es_dst);
   p.vec_dst_t = aligned16(dst_t, ld_dst_t, es_dst);
+  const int st = cast_tma_try(src_dtype, dst_dtype, p, static_cast<cudaStream_t>(stream));
+  if (st != APA_ERR_UNSUPPORTED) return st;
   return cast_dispatch(src_dtype, dst_dtype, p, static_cast<cudaStream_t>(stream));
 }
 

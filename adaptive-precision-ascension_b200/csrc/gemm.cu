@@ -16,6 +16,18 @@
 //               the op's epilogue, store to global; the accumulator is double
 //               buffered so the epilogue of tile i overlaps the MMAs of i+1.
 //
+// CTA-pair variant (PAIR): a cluster of two CTAs on two SMs computes a
+// 256 x BN tile with tcgen05.mma.cta_group::2 (M = 256). Each CTA loads its
+// own 128 rows of A and half (BN/2 rows) of B, so per output element the
+// pair reads 1.5x fewer operand bytes from L2 than two single CTAs. Both
+// CTAs' loads complete on the even CTA's full barrier (the even CTA expects
+// the bytes of both); the even CTA's one MMA thread issues the MMAs, which
+// read both CTAs' shared memory and write each CTA's 128 accumulator rows into
+// its own TMEM; tcgen05.commit multicasts the stage release and the
+// accumulator-ready signal to both CTAs; both CTAs' epilogue warps hand the
+// accumulator back on the even CTA's barrier. Operand loads are plain
+// (non-multicast) TMA loads.
+//
 // Epilogues (the reference's work after each GEMM, fused so no extra pass
 // reads the output back from HBM):
 //   FWD    y = acc + bias (layers.py:164-182), fp32 out (FP8, TF32) or fp16
@@ -56,11 +68,15 @@ template <> struct KindInfo<KIND_TF32> { static constexpr int bytes = 4; static 
 
 constexpr int kEpiStageBytes = 4096;   // per epilogue warp: 32 rows x 128 bytes of output
 
-template <int BN> struct Cfg {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
+// BN: N extent of the output tile; with PAIR each CTA loads BN/2 rows of B.
+template <int BN, bool PAIR = false> struct Cfg {
+  static constexpr int kCtas = PAIR ? 2 : 1;
+  static constexpr int kTileM = BM * kCtas;
+  static constexpr int kBRows = BN / kCtas;
   static constexpr int kABytes = BM * kSlab;
-  static constexpr int kBBytes = BN * kSlab;
+  static constexpr int kBBytes = kBRows * kSlab;
   static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (192 * 1024) / kStageBytes;
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kBarrierBytes = 256;
   static constexpr int kEpiBytes = 4 * kEpiStageBytes + 4 * BN * 4;   // staging + per-warp bias
@@ -100,23 +116,36 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// CLUSTER: acquire at cluster scope, for barriers the peer CTA arrives on.
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
+  if constexpr (CLUSTER) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+  }
   return ok != 0;
 }
 
 // Wait for the phase with the given parity to complete; false after ~2 s.
+template <bool CLUSTER = false>
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int why) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait<CLUSTER>(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
-  while (!mbar_try_wait(bar, parity)) {
+  while (!mbar_try_wait<CLUSTER>(bar, parity)) {
     if (global_ns() - t0 > kWaitLimitNs) {
       atomicOr(&g_status, why);
       return false;
@@ -125,11 +154,46 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
   return true;
 }
 
+// --- cluster (CTA pair) helpers ---
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of every CTA in the cluster; orders shared-memory writes
+// (barrier init, the TMEM address) before the peer's first access.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank`.
+__device__ __forceinline__ uint32_t map_to_cta(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
           smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// CTA-pair load: data into this CTA's shared memory, completion signalled on
+// the mbarrier at `bar_cluster` (the even CTA's barrier). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* tm, int x, int y,
+                                                 uint32_t bar_cluster) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, "
+      "%3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(bar_cluster)
       : "memory");
 }
 
@@ -147,15 +211,32 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
 
 // Instruction descriptor: fp32 accumulator, A/B formats, both K-major,
 // N >> 3 at bit 17, M >> 4 at bit 24.
-template <int KIND, int BN>
+template <int KIND, int BN, int TM = BM>
 __host__ __device__ constexpr uint32_t idesc() {
   return (1u << 4) | (KindInfo<KIND>::fmt << 7) | (KindInfo<KIND>::fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
-         ((uint32_t)(BM >> 4) << 24);
+         ((uint32_t)(TM >> 4) << 24);
 }
 
-template <int KIND>
+template <int KIND, bool PAIR = false>
 __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t accumulate) {
-  if constexpr (KIND == KIND_E4M3) {
+  if constexpr (PAIR) {
+    if constexpr (KIND == KIND_E4M3) {
+      asm volatile(
+          "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+          "l"(a), "l"(b), "r"(id), "r"(accumulate));
+    } else if constexpr (KIND == KIND_F16) {
+      asm volatile(
+          "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+          "l"(a), "l"(b), "r"(id), "r"(accumulate));
+    } else {
+      asm volatile(
+          "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+          "l"(a), "l"(b), "r"(id), "r"(accumulate));
+    }
+  } else if constexpr (KIND == KIND_E4M3) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
@@ -173,9 +254,19 @@ __device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t
   }
 }
 
+template <bool PAIR = false>
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
+  if constexpr (PAIR) {
+    // arrive on the barrier at this offset in both CTAs of the pair
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)0x3)
+        : "memory");
+  } else {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+  }
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -415,11 +506,11 @@ __device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const uint32_t
 // (e.g. a 50k-row vocabulary projection).
 constexpr int kGroupM = 16;
 
-__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& m_blk, int& n_blk) {
-  const int group_tiles = kGroupM * num_n;
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int group, int& m_blk, int& n_blk) {
+  const int group_tiles = group * num_n;
   const int g = tile / group_tiles;
-  const int first_m = g * kGroupM;
-  const int gs = min(kGroupM, num_m - first_m);
+  const int first_m = g * group;
+  const int gs = min(group, num_m - first_m);
   const int local = tile - g * group_tiles;
   m_blk = first_m + local % gs;
   n_blk = local / gs;
@@ -428,11 +519,11 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-template <int KIND, int BN, int EPI>
+template <int KIND, int BN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmO, EpiArgs ea) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, PAIR>;
   constexpr int kStages = C::kStages;
   constexpr int kElemPerSlab = kSlab / KindInfo<KIND>::bytes;
   extern __shared__ uint8_t smem_raw[];
@@ -449,8 +540,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // PAIR: clusters of two CTAs; rank 0 (the even CTA) issues the MMAs
+  const uint32_t rank = PAIR ? cluster_rank() : 0u;
+  const int unit0 = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
+  constexpr int kGroup = PAIR ? kGroupM / 2 : kGroupM;
   const int num_n = (ea.N + BN - 1) / BN;
-  const int num_m = (ea.M + BM - 1) / BM;
+  const int num_m = (ea.M + C::kTileM - 1) / C::kTileM;
   const int num_tiles = num_m * num_n;
   const int kb_count = (int)(((int64_t)ea.K * KindInfo<KIND>::bytes + kSlab - 1) / kSlab);
 
@@ -461,18 +557,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpiThreads);
+      mbar_init(&tempty[a], (kEpiThreads / 32) * C::kCtas);   // one arrival per epilogue warp
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"((uint32_t)C::kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if constexpr (PAIR) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"((uint32_t)C::kTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"((uint32_t)C::kTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
   }
   fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();
+  else __syncthreads();
   fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -481,14 +585,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+      for (int tile = unit0; ok && tile < num_tiles; tile += units) {
         int m_blk, n_blk;
-        tile_coords(tile, num_m, num_n, m_blk, n_blk);
+        tile_coords(tile, num_m, num_n, kGroup, m_blk, n_blk);
+        const int a_row = m_blk * C::kTileM + (int)rank * BM;
+        const int b_row = n_blk * BN + (int)rank * C::kBRows;
         for (int kb = 0; kb < kb_count; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, kStatusTimeoutEmpty)) { ok = false; break; }
-          mbar_expect_tx(&full[stage], C::kStageBytes);
-          tma_load_2d(smA + stage * C::kABytes, &tmA, kb * kElemPerSlab, m_blk * BM, &full[stage]);
-          tma_load_2d(smB + stage * C::kBBytes, &tmB, kb * kElemPerSlab, n_blk * BN, &full[stage]);
+          if constexpr (PAIR) {
+            // the even CTA's full barrier expects both CTAs' bytes
+            if (rank == 0) mbar_expect_tx(&full[stage], C::kCtas * C::kStageBytes);
+            const uint32_t bar = map_to_cta(&full[stage], 0);
+            tma_load_2d_pair(smA + stage * C::kABytes, &tmA, kb * kElemPerSlab, a_row, bar);
+            tma_load_2d_pair(smB + stage * C::kBBytes, &tmB, kb * kElemPerSlab, b_row, bar);
+          } else {
+            mbar_expect_tx(&full[stage], C::kStageBytes);
+            tma_load_2d(smA + stage * C::kABytes, &tmA, kb * kElemPerSlab, a_row, &full[stage]);
+            tma_load_2d(smB + stage * C::kBBytes, &tmB, kb * kElemPerSlab, b_row, &full[stage]);
+          }
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
       }
@@ -501,16 +615,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      constexpr uint32_t id = idesc<KIND, BN>();
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++local) {
+      constexpr uint32_t id = idesc<KIND, BN, C::kTileM>();
+      for (int tile = unit0; ok && tile < num_tiles; tile += units, ++local) {
         const int acc = local & 1;
         const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
-        if (!mbar_wait(&tempty[acc], acc_par ^ 1u, kStatusTimeoutAcc)) { ok = false; break; }
+        if (!mbar_wait<PAIR>(&tempty[acc], acc_par ^ 1u, kStatusTimeoutAcc)) { ok = false; break; }
         fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < kb_count; ++kb) {
@@ -520,11 +634,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b0 = smem_u32(smB + stage * C::kBBytes);
 #pragma unroll
           for (int k = 0; k < kSlab / 32; ++k)
-            mma<KIND>(d, sdesc(a0 + 32 * k), sdesc(b0 + 32 * k), id, (kb | k) != 0 ? 1u : 0u);
-          mma_commit(&empty[stage]);
+            mma<KIND, PAIR>(d, sdesc(a0 + 32 * k), sdesc(b0 + 32 * k), id, (kb | k) != 0 ? 1u : 0u);
+          mma_commit<PAIR>(&empty[stage]);
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
-        if (ok) mma_commit(&tfull[acc]);
+        if (ok) mma_commit<PAIR>(&tfull[acc]);
       }
     }
     __syncwarp();
@@ -538,13 +652,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     EpiState st;
     int local = 0;
     bool pending_store = false;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+    // accumulator hand-back: one arrival per warp on the MMA CTA's barrier
+    const uint32_t tempty0 = PAIR ? map_to_cta(&tempty[0], 0) : 0u;
+    const uint32_t tempty1 = PAIR ? map_to_cta(&tempty[1], 0) : 0u;
+    auto release_acc = [&](int acc) {
+      fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (PAIR) mbar_arrive_cluster(acc ? tempty1 : tempty0);
+        else mbar_arrive(&tempty[acc]);
+      }
+    };
+    for (int tile = unit0; tile < num_tiles; tile += units, ++local) {
       const int acc = local & 1;
       const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
       int m_blk, n_blk;
-      tile_coords(tile, num_m, num_n, m_blk, n_blk);
+      tile_coords(tile, num_m, num_n, kGroup, m_blk, n_blk);
       const int col_base = n_blk * BN;
-      const int row0 = m_blk * BM + q * 32;
+      const int row0 = m_blk * C::kTileM + (int)rank * BM + q * 32;
       const int row = row0 + lane;
       const bool row_ok = row < ea.M;
       const bool check = (row0 + 32 > ea.M) || (col_base + BN > ea.N);
@@ -555,7 +680,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
         }
       }
-      if (!mbar_wait(&tfull[acc], acc_par, kStatusTimeoutAcc)) break;
+      // one lane waits and the warp follows its verdict, so a timeout can
+      // never split the warp ahead of the warp-collective TMEM loads
+      bool ready = true;
+      if (lane == 0) ready = mbar_wait(&tfull[acc], acc_par, kStatusTimeoutAcc);
+      ready = __shfl_sync(0xFFFFFFFFu, ready ? 1 : 0, 0) != 0;
+      if (!ready) break;
       fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
@@ -569,8 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
         if (u == BN / 64 - 1 || col0 + 64 >= ea.N) {
           // every TMEM read of this accumulator is done: hand it back early
-          fence_before();
-          mbar_arrive(&tempty[acc]);
+          release_acc(acc);
         }
         epi_unit<KIND, EPI>(ea, sb + u * 64, r, st, check, row_ok, nv);
         if (ea.tma_out) {
@@ -598,10 +727,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           store_unit_direct(ea, row, col0, nv, r, out16);
         }
       }
-      if (col_base >= ea.N) {   // cannot happen for a valid tile; keep the barrier count exact
-        fence_before();
-        mbar_arrive(&tempty[acc]);
-      }
+      if (col_base >= ea.N) release_acc(acc);   // cannot happen for a valid tile; keep the count exact
     }
     if (pending_store && lane == 0) bulk_wait_all();
     __syncwarp();
@@ -645,13 +771,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  // PAIR: neither CTA leaves (or frees TMEM) while the other may still signal
+  // its barriers or read its accumulators
   fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();
+  else __syncthreads();
   fence_after();
   if (warp == 1) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"((uint32_t)C::kTmemCols)
-                 : "memory");
+    if constexpr (PAIR) {
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"((uint32_t)C::kTmemCols)
+                   : "memory");
+    } else {
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"((uint32_t)C::kTmemCols)
+                   : "memory");
+    }
   }
 }
 
@@ -717,35 +852,93 @@ bool make_out_map(CUtensorMap* tm, const EpiArgs& ea) {
              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Number of two-CTA clusters of this kernel that fit on the device at once
+// (0 when none does), computed once per kernel.
 template <int KIND, int BN, int EPI>
+int pair_capacity() {
+  using C = Cfg<BN, true>;
+  static std::once_flag once;
+  static int clusters = 0;
+  std::call_once(once, [] {
+    if (cudaFuncSetAttribute(gemm_kernel<KIND, BN, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::kSmemBytes) != cudaSuccess)
+      return;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * num_sms(), 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<KIND, BN, EPI, true>, &cfg) == cudaSuccess) clusters = n;
+    else (void)cudaGetLastError();
+  });
+  return clusters;
+}
+
+template <int KIND, int BN, int EPI, bool PAIR>
 int launch_t(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea, int grid_cap, cudaStream_t s) {
-  using C = Cfg<BN>;
+  using C = Cfg<BN, PAIR>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_kernel<KIND, BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    attr_err = cudaFuncSetAttribute(gemm_kernel<KIND, BN, EPI, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     C::kSmemBytes);
   });
   if (attr_err != cudaSuccess) return APA_ERR_CUDA;
   CUtensorMap ta, tb;
   int st = make_map(&ta, KIND, A, ea.M, ea.K, lda, BM);
   if (st) return st;
-  st = make_map(&tb, KIND, B, ea.N, ea.K, ldb, BN);
+  st = make_map(&tb, KIND, B, ea.N, ea.K, ldb, C::kBRows);
   if (st) return st;
   CUtensorMap to = ta;
   ea.tma_out = make_out_map(&to, ea) ? 1 : 0;
-  const int tiles = ((ea.M + BM - 1) / BM) * ((ea.N + BN - 1) / BN);
-  int grid = std::min(tiles, grid_cap > 0 ? grid_cap : num_sms());
-  if (grid < 1) grid = 1;
-  gemm_kernel<KIND, BN, EPI><<<grid, kThreads, C::kSmemBytes, s>>>(ta, tb, to, ea);
+  const int tiles = ((ea.M + C::kTileM - 1) / C::kTileM) * ((ea.N + BN - 1) / BN);
+  if constexpr (PAIR) {
+    const int cap = pair_capacity<KIND, BN, EPI>();
+    if (cap < 1) return APA_ERR_UNSUPPORTED;
+    int clusters = std::min(tiles, grid_cap > 0 ? std::max(1, grid_cap / 2) : cap);
+    clusters = std::max(1, std::min(clusters, cap));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, gemm_kernel<KIND, BN, EPI, true>, ta, tb, to, ea) != cudaSuccess) return APA_ERR_CUDA;
+  } else {
+    int grid = std::min(tiles, grid_cap > 0 ? grid_cap : num_sms());
+    if (grid < 1) grid = 1;
+    gemm_kernel<KIND, BN, EPI, false><<<grid, kThreads, C::kSmemBytes, s>>>(ta, tb, to, ea);
+  }
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }
 
+// Tile shapes: 128 x 128 and 128 x 256 on one CTA, 256 x 256 on a CTA pair.
+constexpr int kTile128 = 128, kTile256 = 256, kTilePair = 512;
+
 template <int KIND, int EPI>
-int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea, int bn, int grid_cap,
+int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea, int tile, int grid_cap,
               cudaStream_t s) {
-  if (bn == 256) return launch_t<KIND, 256, EPI>(A, lda, B, ldb, ea, grid_cap, s);
-  return launch_t<KIND, 128, EPI>(A, lda, B, ldb, ea, grid_cap, s);
+  if (tile == kTilePair) return launch_t<KIND, 256, EPI, true>(A, lda, B, ldb, ea, grid_cap, s);
+  if (tile == kTile256) return launch_t<KIND, 256, EPI, false>(A, lda, B, ldb, ea, grid_cap, s);
+  return launch_t<KIND, 128, EPI, false>(A, lda, B, ldb, ea, grid_cap, s);
+}
+
+template <int KIND, int EPI>
+bool pair_ok() {
+  return pair_capacity<KIND, 256, EPI>() > 0;
 }
 
 }  // namespace gemm
@@ -754,27 +947,48 @@ int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea
 // collective runs concurrently, so its kernel finds free SMs.
 static int g_gemm_sm_limit = 0;
 
-// Choose the N tile: 256 keeps shared-memory traffic per MMA lowest; 128 when
-// N is small or 256-wide tiles would leave SMs idle.
-int pick_bn(int64_t M, int64_t N) {
-  if (N <= 128) return 128;
-  const int64_t t256 = ((M + 127) / 128) * ((N + 255) / 256);
-  if (t256 >= num_sms()) return 256;
-  const int64_t t128 = ((M + 127) / 128) * ((N + 127) / 128);
-  return t128 > t256 ? 128 : 256;
+// Choose the tile shape by an estimate of the persistent schedule's length:
+// waves (work units over the CTAs or pairs that run at once) times the time of
+// one unit. A 128 x 128 unit has half the outputs of a 128 x 256 one but
+// reads more operand bytes per output; a CTA pair reads 1.5x fewer than two
+// single CTAs for the same outputs.
+int pick_tile(int64_t M, int64_t N, int slots, bool pair_possible) {
+  using namespace gemm;
+  auto cdiv = [](int64_t a, int64_t b) { return (a + b - 1) / b; };
+  const int64_t sms = std::max(1, slots);
+  const double t128 = (double)cdiv(cdiv(M, 128) * cdiv(N, 128), sms) * (0.5 / 0.8);
+  const double t256 = (double)cdiv(cdiv(M, 128) * cdiv(N, 256), sms);
+  double best = t256;
+  int tile = kTile256;
+  if (t128 < best) { best = t128; tile = kTile128; }
+  if (pair_possible && M > 128) {
+    const double tp = (double)cdiv(cdiv(M, 256) * cdiv(N, 256), std::max<int64_t>(1, sms / 2)) * (1.0 / 1.15);
+    if (tp < best) { best = tp; tile = kTilePair; }
+  }
+  return tile;
 }
 
 int gemm_dispatch(int rung, int epi, const void* A, int64_t lda, const void* B, int64_t ldb, gemm::EpiArgs ea,
-                  int bn, int grid_cap, cudaStream_t s) {
+                  int tile, int grid_cap, cudaStream_t s) {
   using namespace gemm;
-  if (bn != 128 && bn != 256) bn = pick_bn(ea.M, ea.N);
   if (grid_cap <= 0 && g_gemm_sm_limit > 0) grid_cap = g_gemm_sm_limit;
-#define APA_EPI_CASE(KIND)                                                               \
-  switch (epi) {                                                                          \
-    case EPI_FWD: return launch_bn<KIND, EPI_FWD>(A, lda, B, ldb, ea, bn, grid_cap, s);   \
-    case EPI_DGRAD: return launch_bn<KIND, EPI_DGRAD>(A, lda, B, ldb, ea, bn, grid_cap, s); \
-    case EPI_WGRAD: return launch_bn<KIND, EPI_WGRAD>(A, lda, B, ldb, ea, bn, grid_cap, s); \
-    default: return APA_ERR_INVALID;                                                      \
+#define APA_EPI_CASE(KIND)                                                                                \
+  {                                                                                                        \
+    bool pair = false;                                                                                     \
+    switch (epi) {                                                                                         \
+      case EPI_FWD: pair = pair_ok<KIND, EPI_FWD>(); break;                                                \
+      case EPI_DGRAD: pair = pair_ok<KIND, EPI_DGRAD>(); break;                                            \
+      case EPI_WGRAD: pair = pair_ok<KIND, EPI_WGRAD>(); break;                                            \
+      default: return APA_ERR_INVALID;                                                                     \
+    }                                                                                                      \
+    if (tile == kTilePair && !pair) return APA_ERR_UNSUPPORTED;                                            \
+    if (tile != kTile128 && tile != kTile256 && tile != kTilePair)                                         \
+      tile = pick_tile(ea.M, ea.N, grid_cap > 0 ? grid_cap : num_sms(), pair);                             \
+    switch (epi) {                                                                                         \
+      case EPI_FWD: return launch_bn<KIND, EPI_FWD>(A, lda, B, ldb, ea, tile, grid_cap, s);                \
+      case EPI_DGRAD: return launch_bn<KIND, EPI_DGRAD>(A, lda, B, ldb, ea, tile, grid_cap, s);            \
+      default: return launch_bn<KIND, EPI_WGRAD>(A, lda, B, ldb, ea, tile, grid_cap, s);                   \
+    }                                                                                                      \
   }
   switch (rung) {
     case APA_RUNG_FP8: APA_EPI_CASE(KIND_E4M3)
@@ -863,7 +1077,7 @@ extern "C" int apa_set_gemm_sm_limit(int limit) {
 }
 
 extern "C" int apa_gemm_tn(int rung, int epilogue, const void* A, int64_t lda, const void* B, int64_t ldb, void* out,
-                           int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K, int tile_n, int grid_cap,
+                           int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K, int tile, int grid_cap,
                            void* stream) {
   // Plain D = A . B^T with the epilogue of the given op and no telemetry
   // side effects; used to time the bare GEMM against the fused versions.
@@ -872,5 +1086,5 @@ extern "C" int apa_gemm_tn(int rung, int epilogue, const void* A, int64_t lda, c
   EpiArgs ea = blank(M, N, K);
   ea.out = out; ea.ldo = ldo; ea.out_dt = out_dtype;
   ea.vec_out = out_vec(out, ldo, out_dtype == APA_DT_F32 ? 4 : 2);
-  return apa::gemm_dispatch(rung, epilogue, A, lda, B, ldb, ea, tile_n, grid_cap, static_cast<cudaStream_t>(stream));
+  return apa::gemm_dispatch(rung, epilogue, A, lda, B, ldb, ea, tile, grid_cap, static_cast<cudaStream_t>(stream));
 }

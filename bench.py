@@ -616,6 +616,64 @@ def profile_case(case: str):
             _lib.check(lib.apa_cast(dy.data_ptr(), _lib.DT_F32, M, N, N, dq.data_ptr(), _lib.DT_E4M3, N,
                                     dqt.data_ptr(), M, amax.data_ptr(), flag.data_ptr(), 1, None, part.data_ptr(),
                                     st), "dyprep")
+    elif case in ("step-fp8", "step-fp16", "step-tf32"):
+        # one full APA step (pre_step, forward, backward, ladder) through the
+        # public API, between cudaProfilerStart/Stop after warm-up steps, for
+        # `ncu --profile-from-start off` launch lists
+        import torch.nn as nn
+        from apa import APAConfig, APALinear, APAManager
+        level = {"step-fp8": 0, "step-fp16": 1, "step-tf32": 2}[case]
+        x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16).requires_grad_(True)
+        dy = torch.randn(M, N, device=dev, generator=g)
+        if level == 1:
+            dy = dy.half()
+        cfg = APAConfig(device=str(dev), check_interval=1)
+        torch.manual_seed(0)
+        lin = APALinear(K, N, config=cfg)
+        lin.level = level
+        mgr = APAManager(nn.Sequential(lin), cfg)
+
+        def step():
+            mgr.pre_step()
+            lin(x).backward(dy)
+            x.grad = None
+            mgr.post_backward_sync_and_eval()
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStart()
+        step()
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
+    elif case in ("step-gpt2m", "step-gpt-char"):
+        # one eager GPT training step (pre_step, forward, backward, ladder,
+        # AdamW) between cudaProfilerStart/Stop, after warm-up steps
+        import torch.nn as nn
+        import torch.nn.functional as F
+        import apa
+        from apa import APAManager
+        cfgd = GPT_CONFIGS[case[len("step-"):]]
+        model, cfg = build_gpt(torch, nn, F, apa, cfgd, dev)
+        mgr = APAManager(model, cfg)
+        opt = torch.optim.AdamW(mgr.get_trainable_parameters(), lr=cfgd["lr"], weight_decay=0.01, fused=True)
+        batches = gpt_batches(torch, cfgd, 0, dev)
+        V = cfgd["vocab_pad"]
+
+        def step(i):
+            xb, yb = batches[i % len(batches)]
+            mgr.pre_step()
+            opt.zero_grad(set_to_none=True)
+            loss = F.cross_entropy(model(xb).reshape(-1, V).float(), yb.reshape(-1))
+            loss.backward()
+            if mgr.post_backward_sync_and_eval():
+                opt.step()
+        for i in range(4):
+            step(i)
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStart()
+        step(4)
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
     else:
         raise SystemExit(f"unknown profile case {case}")
     torch.cuda.synchronize()
@@ -635,7 +693,8 @@ def main():
     ap.add_argument("--gpt-steps", type=int, default=10)
     ap.add_argument("--gpt-eager", action="store_true", help="time the GPT workloads without CUDA-graph replay")
     ap.add_argument("--profile-case", default=None,
-                    help="run a few launches of one kernel for an ncu capture (gemm-fp8|gemm-fp16|gemm-tf32|cast|dyprep)")
+                    help="run a few launches of one kernel for an ncu capture (gemm-fp8|gemm-fp16|gemm-tf32|cast|dyprep), "
+                         "or one profiled step (step-fp8|step-fp16|step-tf32|step-gpt2m|step-gpt-char)")
     args = ap.parse_args()
     if args.profile_case:
         profile_case(args.profile_case)

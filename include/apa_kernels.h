@@ -166,12 +166,18 @@ int apa_set_gemm_sm_limit(int limit);
 
 /*
  * The same tcgen05 GEMM with a chosen epilogue and no telemetry side effects,
- * optional N tile (128/256, 0 = automatic) and grid cap (0 = one CTA per SM).
- * Used to time the bare GEMM against the fused entry points.
+ * a chosen tile shape (APA_TILE_*; APA_TILE_AUTO picks one) and grid cap in
+ * CTAs (0 = one CTA per SM). Used to time the bare GEMM against the fused
+ * entry points and to test every tile shape. APA_ERR_UNSUPPORTED when the
+ * CTA-pair shape cannot be launched on this device.
  */
+#define APA_TILE_AUTO 0
+#define APA_TILE_128x128 128      /* one CTA per tile */
+#define APA_TILE_128x256 256      /* one CTA per tile */
+#define APA_TILE_PAIR_256x256 512 /* a cluster of two CTAs, tcgen05 cta_group::2 */
 int apa_gemm_tn(int rung, int epilogue, const void* A, int64_t lda, const void* B, int64_t ldb,
                 void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
-                int tile_n, int grid_cap, void* stream);
+                int tile, int grid_cap, void* stream);
 
 /*
  * Bias gradient without any device allocation: db[c] = f32(cast(sum_r
