@@ -12,9 +12,12 @@
 //               kStages-deep shared-memory ring (mbarrier full/empty pairs)
 //   warp 1      allocates 2*BN TMEM columns; one thread issues tcgen05.mma
 //               (4 per 128-byte K slab) and tcgen05.commit to release stages
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time, apply
-//               the op's epilogue, store to global; the accumulator is double
-//               buffered so the epilogue of tile i overlaps the MMAs of i+1.
+//   warps 2..9  epilogue: two warps per TMEM lane quarter, each taking half
+//               of the tile's columns; tcgen05.ld 32 lanes x 32 columns at a
+//               time, apply the op's epilogue, stage 32 x 128-byte boxes in a
+//               small ring of shared-memory buffers and write them with TMA
+//               bulk-tensor stores; the accumulator is double buffered so the
+//               epilogue of tile i overlaps the MMAs of i+1.
 //
 // CTA-pair variant (PAIR): a cluster of two CTAs on two SMs computes a
 // 256 x BN tile with tcgen05.mma.cta_group::2 (M = 256). Each CTA loads its
@@ -55,8 +58,12 @@ namespace gemm {
 
 constexpr int BM = 128;
 constexpr int kSlab = 128;            // K bytes per pipeline stage (one swizzle row)
-constexpr int kThreads = 192;
-constexpr int kEpiThreads = 128;
+// Epilogue warps EW = 4 or 8: warp w may only read TMEM lanes 32*(w%4) ..
+// +31, so each lane quarter (32 accumulator rows) gets EW/4 warps that split
+// the tile's columns between them. 8 warps when the epilogue cannot hide
+// behind the next tile's MMAs (short K, or one or two tiles per CTA); 4 warps
+// and a deeper operand pipeline otherwise.
+template <int EW> constexpr int threads_for() { return 64 + 32 * EW; }
 
 enum { KIND_E4M3 = 0, KIND_F16 = 1, KIND_TF32 = 2 };
 enum { EPI_FWD = 0, EPI_DGRAD = 1, EPI_WGRAD = 2 };
@@ -66,20 +73,29 @@ template <> struct KindInfo<KIND_E4M3> { static constexpr int bytes = 1; static 
 template <> struct KindInfo<KIND_F16> { static constexpr int bytes = 2; static constexpr uint32_t fmt = 0; };
 template <> struct KindInfo<KIND_TF32> { static constexpr int bytes = 4; static constexpr uint32_t fmt = 2; };
 
-constexpr int kEpiStageBytes = 4096;   // per epilogue warp: 32 rows x 128 bytes of output
+constexpr int kEpiStageBytes = 4096;   // one staging buffer: 32 rows x 128 bytes of output
+
 
 // BN: N extent of the output tile; with PAIR each CTA loads BN/2 rows of B.
-template <int BN, bool PAIR = false> struct Cfg {
+// Pipeline depth and staging buffers per epilogue warp, per shape: the
+// staging ring lets a warp fill the next buffer while earlier TMA stores are
+// still reading theirs.
+template <int BN, bool PAIR, int EW> struct Cfg {
   static constexpr int kCtas = PAIR ? 2 : 1;
   static constexpr int kTileM = BM * kCtas;
   static constexpr int kBRows = BN / kCtas;
   static constexpr int kABytes = BM * kSlab;
   static constexpr int kBBytes = kBRows * kSlab;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (192 * 1024) / kStageBytes;
+  static constexpr int kStages = EW == 8 ? (PAIR ? 4 : (BN == 256 ? 3 : 4)) : (PAIR ? 6 : (BN == 256 ? 4 : 6));
   static constexpr int kTmemCols = 2 * BN;
   static constexpr int kBarrierBytes = 256;
-  static constexpr int kEpiBytes = 4 * kEpiStageBytes + 4 * BN * 4;   // staging + per-warp bias
+  static constexpr int kEpiWarps = EW;
+  static constexpr int kEpiThreads = 32 * EW;
+  static constexpr int kThreads = threads_for<EW>();
+  static constexpr int kEpiBufs = EW == 8 ? 2 : 1;
+  static constexpr int kWarpCols = BN / (EW / 4);                      // columns per epilogue warp
+  static constexpr int kEpiBytes = EW * kEpiBufs * kEpiStageBytes + EW * kWarpCols * 4;
   static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + kBarrierBytes + 1024;
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -311,7 +327,10 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* tm, const void* 
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -519,11 +538,13 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int 
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-template <int KIND, int BN, int EPI, bool PAIR>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int KIND, int BN, int EPI, bool PAIR, int EW>
+__global__ void __launch_bounds__(threads_for<EW>(), 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmO, EpiArgs ea) {
-  using C = Cfg<BN, PAIR>;
+  using C = Cfg<BN, PAIR, EW>;
+  constexpr int kEpiWarps = C::kEpiWarps;
+  constexpr int kEpiThreads = C::kEpiThreads;
   constexpr int kStages = C::kStages;
   constexpr int kElemPerSlab = kSlab / KindInfo<KIND>::bytes;
   extern __shared__ uint8_t smem_raw[];
@@ -531,9 +552,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* smA = smem;
   uint8_t* smB = smem + kStages * C::kABytes;
-  uint8_t* sEpi = smem + kStages * C::kStageBytes;                 // 4 warps x 4 KB staging
-  float* sBias = reinterpret_cast<float*>(sEpi + 4 * kEpiStageBytes);   // 4 warps x BN floats
-  uint64_t* full = reinterpret_cast<uint64_t*>(sBias + 4 * BN);
+  uint8_t* sEpi = smem + kStages * C::kStageBytes;                 // per warp: kEpiBufs x 4 KB staging
+  float* sBias = reinterpret_cast<float*>(sEpi + kEpiWarps * C::kEpiBufs * kEpiStageBytes);   // per warp: its columns
+  uint64_t* full = reinterpret_cast<uint64_t*>(sBias + kEpiWarps * C::kWarpCols);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;
   uint64_t* tempty = tfull + 2;
@@ -557,7 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], (kEpiThreads / 32) * C::kCtas);   // one arrival per epilogue warp
+      mbar_init(&tempty[a], kEpiWarps * C::kCtas);   // one arrival per epilogue warp
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -643,15 +664,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else {
-    // epilogue warps 2..5 -> TMEM lane quarters 2,3,0,1
+    // epilogue warps 2 .. 2+kEpiWarps-1: TMEM lane quarter warp%4, column
+    // part (warp-2)/4 of the tile
     const int q = warp & 3;
     const int e = warp - 2;
-    uint8_t* stage_buf = sEpi + e * kEpiStageBytes;
-    float* sb = sBias + e * BN;
+    const int part = e >> 2;
+    constexpr int kUnits = C::kWarpCols / 64;                // 64-column units per warp
+    uint8_t* stage_base = sEpi + e * C::kEpiBufs * kEpiStageBytes;
+    float* sb = sBias + e * C::kWarpCols;
     const bool out16 = ea.out_dt != APA_DT_F32;
     EpiState st;
     int local = 0;
-    bool pending_store = false;
+    int slot = 0, inflight = 0;   // staging ring position, stores not yet known to be read
     // accumulator hand-back: one arrival per warp on the MMA CTA's barrier
     const uint32_t tempty0 = PAIR ? map_to_cta(&tempty[0], 0) : 0u;
     const uint32_t tempty1 = PAIR ? map_to_cta(&tempty[1], 0) : 0u;
@@ -668,14 +692,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
       int m_blk, n_blk;
       tile_coords(tile, num_m, num_n, kGroup, m_blk, n_blk);
-      const int col_base = n_blk * BN;
+      const int col_base = n_blk * BN + part * C::kWarpCols;   // this warp's first column
       const int row0 = m_blk * C::kTileM + (int)rank * BM + q * 32;
       const int row = row0 + lane;
       const bool row_ok = row < ea.M;
-      const bool check = (row0 + 32 > ea.M) || (col_base + BN > ea.N);
+      const bool check = (row0 + 32 > ea.M) || (col_base + C::kWarpCols > ea.N);
       if constexpr (EPI == EPI_FWD) {
         if (ea.bias != nullptr) {
-          for (int c = lane; c < BN; c += 32)
+          for (int c = lane; c < C::kWarpCols; c += 32)
             sb[c] = (col_base + c < ea.N) ? bias_value<KIND>(ea.bias, col_base + c) : 0.0f;
           __syncwarp();
         }
@@ -687,9 +711,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       ready = __shfl_sync(0xFFFFFFFFu, ready ? 1 : 0, 0) != 0;
       if (!ready) break;
       fence_after();
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const uint32_t tbase =
+          tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN) + (uint32_t)(part * C::kWarpCols);
+      bool released = false;
 #pragma unroll 1
-      for (int u = 0; u < BN / 64; ++u) {
+      for (int u = 0; u < kUnits; ++u) {
         const int col0 = col_base + u * 64;
         if (col0 >= ea.N) break;   // warp-uniform
         const int nv = min(64, ea.N - col0);
@@ -697,9 +723,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32_nowait(tbase + (uint32_t)(u * 64), r);
         tmem_ld32_nowait(tbase + (uint32_t)(u * 64 + 32), r + 32);
         tmem_wait_ld();
-        if (u == BN / 64 - 1 || col0 + 64 >= ea.N) {
-          // every TMEM read of this accumulator is done: hand it back early
+        if (u == kUnits - 1 || col0 + 64 >= ea.N) {
+          // every TMEM read of this warp's part of the accumulator is done
           release_acc(acc);
+          released = true;
         }
         epi_unit<KIND, EPI>(ea, sb + u * 64, r, st, check, row_ok, nv);
         if (ea.tma_out) {
@@ -709,26 +736,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int b = 0; b < 2; ++b) {
               const int x = col0 + b * 32;
               if (b >= nbox || x >= ea.N) break;
-              if (pending_store) {
-                if (lane == 0) bulk_wait_read_all();
+              if (inflight >= C::kEpiBufs) {
+                // the store that last used this slot must have read it
+                if (lane == 0) bulk_wait_read<C::kEpiBufs - 1>();
                 __syncwarp();
+                inflight = C::kEpiBufs - 1;
               }
-              stage_row(stage_buf, lane, r + 32 * b);
+              uint8_t* buf = stage_base + slot * kEpiStageBytes;
+              stage_row(buf, lane, r + 32 * b);
               fence_async_smem();
               __syncwarp();
               if (lane == 0) {
-                tma_store_2d(&tmO, stage_buf, x, row0);
+                tma_store_2d(&tmO, buf, x, row0);
                 bulk_commit();
               }
-              pending_store = true;
+              ++inflight;
+              slot = slot + 1 == C::kEpiBufs ? 0 : slot + 1;
             }
           }
         } else if (row_ok) {
           store_unit_direct(ea, row, col0, nv, r, out16);
         }
       }
-      if (col_base >= ea.N) release_acc(acc);   // cannot happen for a valid tile; keep the count exact
+      if (!released) release_acc(acc);   // this warp's columns lie past N: keep the count exact
     }
+    const bool pending_store = inflight > 0;
     if (pending_store && lane == 0) bulk_wait_all();
     __syncwarp();
     // per-warp telemetry commit
@@ -748,7 +780,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0 && m != 0u) telem_commit(ea.amax, ea.flag, final_mag<KIND, EPI>(m));
     }
     if constexpr (EPI == EPI_WGRAD) {
-      // named barrier over the 4 epilogue warps, then one ticket per CTA
+      // named barrier over the epilogue warps, then one ticket per CTA
       asm volatile("bar.sync 1, %0;" ::"r"(kEpiThreads) : "memory");
       if (threadIdx.x == 64 && ea.counters) {
         __threadfence();
@@ -854,18 +886,18 @@ bool make_out_map(CUtensorMap* tm, const EpiArgs& ea) {
 
 // Number of two-CTA clusters of this kernel that fit on the device at once
 // (0 when none does), computed once per kernel.
-template <int KIND, int BN, int EPI>
+template <int KIND, int BN, int EPI, int EW>
 int pair_capacity() {
-  using C = Cfg<BN, true>;
+  using C = Cfg<BN, true, EW>;
   static std::once_flag once;
   static int clusters = 0;
   std::call_once(once, [] {
-    if (cudaFuncSetAttribute(gemm_kernel<KIND, BN, EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(gemm_kernel<KIND, BN, EPI, true, EW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::kSmemBytes) != cudaSuccess)
       return;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * num_sms(), 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(C::kThreads, 1, 1);
     cfg.dynamicSmemBytes = C::kSmemBytes;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -875,20 +907,20 @@ int pair_capacity() {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<KIND, BN, EPI, true>, &cfg) == cudaSuccess) clusters = n;
+    if (cudaOccupancyMaxActiveClusters(&n, gemm_kernel<KIND, BN, EPI, true, EW>, &cfg) == cudaSuccess) clusters = n;
     else (void)cudaGetLastError();
   });
   return clusters;
 }
 
-template <int KIND, int BN, int EPI, bool PAIR>
+template <int KIND, int BN, int EPI, bool PAIR, int EW>
 int launch_t(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea, int grid_cap, cudaStream_t s) {
-  using C = Cfg<BN, PAIR>;
+  using C = Cfg<BN, PAIR, EW>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(gemm_kernel<KIND, BN, EPI, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    C::kSmemBytes);
+    attr_err = cudaFuncSetAttribute(gemm_kernel<KIND, BN, EPI, PAIR, EW>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
   });
   if (attr_err != cudaSuccess) return APA_ERR_CUDA;
   CUtensorMap ta, tb;
@@ -900,13 +932,13 @@ int launch_t(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea,
   ea.tma_out = make_out_map(&to, ea) ? 1 : 0;
   const int tiles = ((ea.M + C::kTileM - 1) / C::kTileM) * ((ea.N + BN - 1) / BN);
   if constexpr (PAIR) {
-    const int cap = pair_capacity<KIND, BN, EPI>();
+    const int cap = pair_capacity<KIND, BN, EPI, EW>();
     if (cap < 1) return APA_ERR_UNSUPPORTED;
     int clusters = std::min(tiles, grid_cap > 0 ? std::max(1, grid_cap / 2) : cap);
     clusters = std::max(1, std::min(clusters, cap));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(C::kThreads, 1, 1);
     cfg.dynamicSmemBytes = C::kSmemBytes;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -916,29 +948,39 @@ int launch_t(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea,
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, gemm_kernel<KIND, BN, EPI, true>, ta, tb, to, ea) != cudaSuccess) return APA_ERR_CUDA;
+    if (cudaLaunchKernelEx(&cfg, gemm_kernel<KIND, BN, EPI, true, EW>, ta, tb, to, ea) != cudaSuccess)
+      return APA_ERR_CUDA;
   } else {
     int grid = std::min(tiles, grid_cap > 0 ? grid_cap : num_sms());
     if (grid < 1) grid = 1;
-    gemm_kernel<KIND, BN, EPI, false><<<grid, kThreads, C::kSmemBytes, s>>>(ta, tb, to, ea);
+    gemm_kernel<KIND, BN, EPI, false, EW><<<grid, C::kThreads, C::kSmemBytes, s>>>(ta, tb, to, ea);
   }
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }
 
-// Tile shapes: 128 x 128 and 128 x 256 on one CTA, 256 x 256 on a CTA pair.
+// Tile shapes: 128 x 128 and 128 x 256 on one CTA, 256 x 256 on a CTA pair;
+// flag bits select the epilogue width (0 = automatic).
 constexpr int kTile128 = 128, kTile256 = 256, kTilePair = 512;
+constexpr int kEpiFlag4 = 1, kEpiFlag8 = 2;
+
+template <int KIND, int EPI, int EW>
+int launch_shape(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea, int tile, int grid_cap,
+                 cudaStream_t s) {
+  if (tile == kTilePair) return launch_t<KIND, 256, EPI, true, EW>(A, lda, B, ldb, ea, grid_cap, s);
+  if (tile == kTile256) return launch_t<KIND, 256, EPI, false, EW>(A, lda, B, ldb, ea, grid_cap, s);
+  return launch_t<KIND, 128, EPI, false, EW>(A, lda, B, ldb, ea, grid_cap, s);
+}
 
 template <int KIND, int EPI>
-int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea, int tile, int grid_cap,
+int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea, int tile, int ew, int grid_cap,
               cudaStream_t s) {
-  if (tile == kTilePair) return launch_t<KIND, 256, EPI, true>(A, lda, B, ldb, ea, grid_cap, s);
-  if (tile == kTile256) return launch_t<KIND, 256, EPI, false>(A, lda, B, ldb, ea, grid_cap, s);
-  return launch_t<KIND, 128, EPI, false>(A, lda, B, ldb, ea, grid_cap, s);
+  if (ew == 8) return launch_shape<KIND, EPI, 8>(A, lda, B, ldb, ea, tile, grid_cap, s);
+  return launch_shape<KIND, EPI, 4>(A, lda, B, ldb, ea, tile, grid_cap, s);
 }
 
 template <int KIND, int EPI>
 bool pair_ok() {
-  return pair_capacity<KIND, 256, EPI>() > 0;
+  return pair_capacity<KIND, 256, EPI, 4>() > 0 && pair_capacity<KIND, 256, EPI, 8>() > 0;
 }
 
 }  // namespace gemm
@@ -947,54 +989,109 @@ bool pair_ok() {
 // collective runs concurrently, so its kernel finds free SMs.
 static int g_gemm_sm_limit = 0;
 
-// Choose the tile shape by an estimate of the persistent schedule's length:
-// waves (work units over the CTAs or pairs that run at once) times the time of
-// one unit. A 128 x 128 unit has half the outputs of a 128 x 256 one but
-// reads more operand bytes per output; a CTA pair reads 1.5x fewer than two
-// single CTAs for the same outputs.
-int pick_tile(int64_t M, int64_t N, int slots, bool pair_possible) {
+struct GemmPlan {
+  int tile, ew;
+};
+
+// Tile shape and epilogue width from an estimate of the persistent
+// schedule's length: waves (work units over the CTAs or pairs that run at
+// once) times the cost of one unit. Two regimes:
+//  * epilogue-bound (few 128-byte K slabs per tile for the bytes each output
+//    element stores): a unit costs its valid output columns; a 128-wide unit
+//    0.55 of a 256-wide one (half the outputs plus fixed per-tile work); a
+//    CTA pair gains nothing;
+//  * mainloop-bound: a 128-wide unit costs 0.7 of a 256-wide one (it reads more
+//    operand bytes per output); a CTA pair reads 1.5x fewer operand bytes than
+//    two single CTAs, worth ~8 % once each pair runs three or more tiles (in
+//    one or two waves the cluster's lock-step loads cost as much).
+// Eight epilogue warps when the epilogue is exposed: epilogue-bound shapes,
+// and any schedule of at most two tiles per CTA (the last tile's epilogue
+// follows no MMAs); otherwise four warps and a deeper operand pipeline.
+GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int es, int out_es, int slots, bool pair_possible, int tile) {
   using namespace gemm;
   auto cdiv = [](int64_t a, int64_t b) { return (a + b - 1) / b; };
   const int64_t sms = std::max(1, slots);
-  const double t128 = (double)cdiv(cdiv(M, 128) * cdiv(N, 128), sms) * (0.5 / 0.8);
-  const double t256 = (double)cdiv(cdiv(M, 128) * cdiv(N, 256), sms);
-  double best = t256;
-  int tile = kTile256;
-  if (t128 < best) { best = t128; tile = kTile128; }
-  if (pair_possible && M > 128) {
-    const double tp = (double)cdiv(cdiv(M, 256) * cdiv(N, 256), std::max<int64_t>(1, sms / 2)) * (1.0 / 1.15);
-    if (tp < best) { best = tp; tile = kTilePair; }
+  const int64_t k_bytes = K * es;
+  const bool epi_bound = k_bytes * 4 <= 2048 * (int64_t)out_es;
+  auto width = [&](int bn) { return epi_bound ? (double)N / (double)(cdiv(N, bn) * bn) : 1.0; };
+  const int64_t tiles128 = cdiv(M, 128) * cdiv(N, 128);
+  const int64_t tiles256 = cdiv(M, 128) * cdiv(N, 256);
+  const int64_t tilesP = cdiv(M, 256) * cdiv(N, 256);
+  const int64_t pairs = std::max<int64_t>(1, sms / 2);
+  if (tile != kTile128 && tile != kTile256 && tile != kTilePair) {
+    const double t128 = (double)cdiv(tiles128, sms) * width(128) * (epi_bound ? 0.55 : 0.7);
+    const double t256 = (double)cdiv(tiles256, sms) * width(256);
+    double best = t256;
+    tile = kTile256;
+    if (t128 < best) { best = t128; tile = kTile128; }
+    if (pair_possible && M > 128) {
+      const int64_t w = cdiv(tilesP, pairs);
+      const double gain = (!epi_bound && w >= 3) ? 1.0 / 1.08 : 1.0 / 0.97;
+      const double tp = (double)w * width(256) * gain;
+      if (tp < best) { best = tp; tile = kTilePair; }
+    }
   }
-  return tile;
+  const int64_t per_cta = tile == kTilePair ? cdiv(tilesP, pairs) : cdiv(tile == kTile128 ? tiles128 : tiles256, sms);
+  const int ew = (epi_bound || per_cta <= 2) ? 8 : 4;
+  return {tile, ew};
+}
+
+// Whether the CTA-pair kernels of this rung / epilogue can run on the device.
+bool pair_possible(int rung, int epi) {
+  using namespace gemm;
+#define APA_PAIR_CASE(KIND)                                  \
+  switch (epi) {                                             \
+    case EPI_FWD: return pair_ok<KIND, EPI_FWD>();           \
+    case EPI_DGRAD: return pair_ok<KIND, EPI_DGRAD>();       \
+    case EPI_WGRAD: return pair_ok<KIND, EPI_WGRAD>();       \
+    default: return false;                                   \
+  }
+  switch (rung) {
+    case APA_RUNG_FP8: APA_PAIR_CASE(KIND_E4M3)
+    case APA_RUNG_FP16: APA_PAIR_CASE(KIND_F16)
+    case APA_RUNG_TF32: APA_PAIR_CASE(KIND_TF32)
+    default: return false;
+  }
+#undef APA_PAIR_CASE
+}
+
+// The launch configuration of one GEMM: tile code (possibly with epilogue
+// flag bits) and grid cap resolved exactly as gemm_dispatch resolves them.
+int resolve_plan(int rung, int epi, int64_t M, int64_t N, int64_t K, int out_dt, int tile, int grid_cap,
+                 GemmPlan* out) {
+  using namespace gemm;
+  if (rung != APA_RUNG_FP8 && rung != APA_RUNG_FP16 && rung != APA_RUNG_TF32) return APA_ERR_INVALID;
+  if (epi != EPI_FWD && epi != EPI_DGRAD && epi != EPI_WGRAD) return APA_ERR_INVALID;
+  if (grid_cap <= 0 && g_gemm_sm_limit > 0) grid_cap = g_gemm_sm_limit;
+  const int ew_flag = tile & 3;
+  tile &= ~3;
+  const bool pair = pair_possible(rung, epi);
+  if (tile == kTilePair && !pair) return APA_ERR_UNSUPPORTED;
+  const int es = rung == APA_RUNG_FP8 ? 1 : rung == APA_RUNG_FP16 ? 2 : 4;
+  const int out_es = out_dt == APA_DT_F32 ? 4 : 2;
+  GemmPlan pl = plan_gemm(M, N, K, es, out_es, grid_cap > 0 ? grid_cap : num_sms(), pair, tile);
+  if (ew_flag == kEpiFlag4) pl.ew = 4;
+  if (ew_flag == kEpiFlag8) pl.ew = 8;
+  *out = pl;
+  return APA_OK;
 }
 
 int gemm_dispatch(int rung, int epi, const void* A, int64_t lda, const void* B, int64_t ldb, gemm::EpiArgs ea,
                   int tile, int grid_cap, cudaStream_t s) {
   using namespace gemm;
+  GemmPlan pl;
+  if (int st = resolve_plan(rung, epi, ea.M, ea.N, ea.K, ea.out_dt, tile, grid_cap, &pl)) return st;
   if (grid_cap <= 0 && g_gemm_sm_limit > 0) grid_cap = g_gemm_sm_limit;
 #define APA_EPI_CASE(KIND)                                                                                \
-  {                                                                                                        \
-    bool pair = false;                                                                                     \
-    switch (epi) {                                                                                         \
-      case EPI_FWD: pair = pair_ok<KIND, EPI_FWD>(); break;                                                \
-      case EPI_DGRAD: pair = pair_ok<KIND, EPI_DGRAD>(); break;                                            \
-      case EPI_WGRAD: pair = pair_ok<KIND, EPI_WGRAD>(); break;                                            \
-      default: return APA_ERR_INVALID;                                                                     \
-    }                                                                                                      \
-    if (tile == kTilePair && !pair) return APA_ERR_UNSUPPORTED;                                            \
-    if (tile != kTile128 && tile != kTile256 && tile != kTilePair)                                         \
-      tile = pick_tile(ea.M, ea.N, grid_cap > 0 ? grid_cap : num_sms(), pair);                             \
-    switch (epi) {                                                                                         \
-      case EPI_FWD: return launch_bn<KIND, EPI_FWD>(A, lda, B, ldb, ea, tile, grid_cap, s);                \
-      case EPI_DGRAD: return launch_bn<KIND, EPI_DGRAD>(A, lda, B, ldb, ea, tile, grid_cap, s);            \
-      default: return launch_bn<KIND, EPI_WGRAD>(A, lda, B, ldb, ea, tile, grid_cap, s);                   \
-    }                                                                                                      \
+  switch (epi) {                                                                                           \
+    case EPI_FWD: return launch_bn<KIND, EPI_FWD>(A, lda, B, ldb, ea, pl.tile, pl.ew, grid_cap, s);        \
+    case EPI_DGRAD: return launch_bn<KIND, EPI_DGRAD>(A, lda, B, ldb, ea, pl.tile, pl.ew, grid_cap, s);    \
+    default: return launch_bn<KIND, EPI_WGRAD>(A, lda, B, ldb, ea, pl.tile, pl.ew, grid_cap, s);           \
   }
   switch (rung) {
     case APA_RUNG_FP8: APA_EPI_CASE(KIND_E4M3)
     case APA_RUNG_FP16: APA_EPI_CASE(KIND_F16)
-    case APA_RUNG_TF32: APA_EPI_CASE(KIND_TF32)
-    default: return APA_ERR_INVALID;
+    default: APA_EPI_CASE(KIND_TF32)
   }
 #undef APA_EPI_CASE
 }
@@ -1068,6 +1165,17 @@ extern "C" int apa_linear_wgrad(int rung, const void* dyqt, int64_t lddyt, const
   ea.vmin = rung == APA_RUNG_FP8 ? 0.015625f : rung == APA_RUNG_FP16 ? 6.1035e-5f : 0.0f;
   return apa::gemm_dispatch(rung, apa::gemm::EPI_WGRAD, dyqt, lddyt, xqt, ldxt, ea, 0, 0,
                             static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int apa_gemm_plan(int rung, int epilogue, int64_t M, int64_t N, int64_t K, int out_dtype, int tile,
+                             int grid_cap, int* tile_out, int* epi_warps_out) {
+  if (!tile_out || !epi_warps_out) return APA_ERR_INVALID;
+  if (int st = check_dims(M, N, K)) return st;
+  apa::GemmPlan pl;
+  if (int st = apa::resolve_plan(rung, epilogue, M, N, K, out_dtype, tile, grid_cap, &pl)) return st;
+  *tile_out = pl.tile;
+  *epi_warps_out = pl.ew;
+  return APA_OK;
 }
 
 extern "C" int apa_set_gemm_sm_limit(int limit) {

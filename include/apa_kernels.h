@@ -175,9 +175,24 @@ int apa_set_gemm_sm_limit(int limit);
 #define APA_TILE_128x128 128      /* one CTA per tile */
 #define APA_TILE_128x256 256      /* one CTA per tile */
 #define APA_TILE_PAIR_256x256 512 /* a cluster of two CTAs, tcgen05 cta_group::2 */
+/* OR-ed into the tile code: the number of epilogue warps (default: chosen
+ * with the tile, 8 when the epilogue cannot hide behind the MMAs) */
+#define APA_TILE_EPI_WARPS_4 1
+#define APA_TILE_EPI_WARPS_8 2
 int apa_gemm_tn(int rung, int epilogue, const void* A, int64_t lda, const void* B, int64_t ldb,
                 void* out, int out_dtype, int64_t ldo, int64_t M, int64_t N, int64_t K,
                 int tile, int grid_cap, void* stream);
+
+/*
+ * The launch configuration a GEMM of this shape would use (apa_linear_* pass
+ * APA_TILE_AUTO and grid cap 0; M, N, K as in apa_gemm_tn, i.e. for dgrad
+ * M = tokens, N = in features, K = out features and for wgrad M = out
+ * features, N = in features, K = tokens): *tile_out = 128, 256 or 512
+ * (APA_TILE_*), *epi_warps_out = 4 or 8. Launches nothing. No counterpart in
+ * the reference.
+ */
+int apa_gemm_plan(int rung, int epilogue, int64_t M, int64_t N, int64_t K, int out_dtype, int tile,
+                  int grid_cap, int* tile_out, int* epi_warps_out);
 
 /*
  * Bias gradient without any device allocation: db[c] = f32(cast(sum_r
