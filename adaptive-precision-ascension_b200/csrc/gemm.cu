@@ -65,6 +65,7 @@ constexpr int kSlab = 128;            // K bytes per pipeline stage (one swizzle
 // and a deeper operand pipeline otherwise.
 template <int EW> constexpr int threads_for() { return 64 + 32 * EW; }
 
+
 enum { KIND_E4M3 = 0, KIND_F16 = 1, KIND_TF32 = 2 };
 enum { EPI_FWD = 0, EPI_DGRAD = 1, EPI_WGRAD = 2 };
 
@@ -103,6 +104,7 @@ template <int BN, bool PAIR, int EW> struct Cfg {
 struct EpiArgs {
   void* out; int64_t ldo; int out_dt; int vec_out;
   int tma_out;                      // output written by TMA bulk-tensor stores
+  int coalesced_out;                // output written by store_box_coalesced
   const void* bias;                 // FWD: working-dtype bias (nullable)
   float* amax; int* flag;           // FWD: module telemetry; DGRAD: boundary_cast telemetry
   unsigned long long* counters;     // WGRAD: [nonzero, underflow, ticket], zero on entry
@@ -519,6 +521,51 @@ __device__ __forceinline__ void stage_row(uint8_t* buf, int lane, const uint32_t
         make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
 }
 
+// Store one 32-row x 128-byte box from registers (lane = row, w[0..31] = the
+// row's 32 words) without the TMA unit: stage the rows in the warp's buffer
+// (swizzled, conflict-free), read them back so that lane l holds 16-byte
+// chunk l%8 of row 4i + l/8, and store: every warp instruction then writes
+// four full 128-byte rows. The buffer is free again when this returns.
+// accumulate: add the existing fp32 values (read the same way).
+__device__ __forceinline__ void store_box_coalesced(const EpiArgs& ea, uint8_t* buf, int lane, const uint32_t* w,
+                                                    int row0, int x, int es) {
+  stage_row(buf, lane, w);
+  __syncwarp();
+  const int c = lane & 7;
+  const int per = 16 / es;   // elements per chunk
+  const int col = x + c * per;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (lane >> 3);
+    uint4 v = *reinterpret_cast<const uint4*>(buf + r * 128 + ((c ^ (r & 7)) << 4));
+    const int grow = row0 + r;
+    if (grow < ea.M && col < ea.N) {
+      uint8_t* dst = static_cast<uint8_t*>(ea.out) + ((int64_t)grow * ea.ldo + col) * es;
+      if (col + per <= ea.N) {
+        if (ea.accumulate) {
+          const float4 o = *reinterpret_cast<const float4*>(dst);
+          v.x = __float_as_uint(o.x + fu(v.x));
+          v.y = __float_as_uint(o.y + fu(v.y));
+          v.z = __float_as_uint(o.z + fu(v.z));
+          v.w = __float_as_uint(o.w + fu(v.w));
+        }
+        *reinterpret_cast<uint4*>(dst) = v;
+      } else {
+        const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+        for (int e = 0; e < per && col + e < ea.N; ++e) {
+          if (es == 4) {
+            float* d = reinterpret_cast<float*>(dst) + e;
+            *d = ea.accumulate ? *d + fu(vw[e]) : fu(vw[e]);
+          } else {
+            reinterpret_cast<uint16_t*>(dst)[e] = (uint16_t)(vw[e >> 1] >> (16 * (e & 1)));
+          }
+        }
+      }
+    }
+  }
+  __syncwarp();
+}
+
 // Tile order: groups of kGroupM consecutive M blocks, N advancing across a
 // group and M fastest inside it, so the CTAs running at the same time share
 // their B tiles (and a group's A rows) in L2 even when B is larger than L2
@@ -729,7 +776,17 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
           released = true;
         }
         epi_unit<KIND, EPI>(ea, sb + u * 64, r, st, check, row_ok, nv);
-        if (ea.tma_out) {
+        if (ea.coalesced_out) {
+          if (row0 < ea.M) {
+            const int nbox = out16 ? 1 : 2;
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+              const int x = col0 + b * 32;
+              if (b >= nbox || x >= ea.N) break;
+              store_box_coalesced(ea, stage_base, lane, r + 32 * b, row0, out16 ? col0 : x, out16 ? 2 : 4);
+            }
+          }
+        } else if (ea.tma_out) {
           if (row0 < ea.M) {
             const int nbox = out16 ? 1 : 2;
 #pragma unroll
@@ -929,7 +986,11 @@ int launch_t(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea,
   st = make_map(&tb, KIND, B, ea.N, ea.K, ldb, C::kBRows);
   if (st) return st;
   CUtensorMap to = ta;
+  // aligned outputs: TMA bulk-tensor stores (measured faster than coalesced
+  // st.global from the same staging); accumulating into an aligned fp32
+  // gradient: coalesced read-add-store through the staging buffer
   ea.tma_out = make_out_map(&to, ea) ? 1 : 0;
+  ea.coalesced_out = (!ea.tma_out && ea.accumulate && ea.vec_out) ? 1 : 0;
   const int tiles = ((ea.M + C::kTileM - 1) / C::kTileM) * ((ea.N + BN - 1) / BN);
   if constexpr (PAIR) {
     const int cap = pair_capacity<KIND, BN, EPI, EW>();
@@ -1110,7 +1171,7 @@ int check_dims(int64_t M, int64_t N, int64_t K) {
 
 EpiArgs blank(int64_t M, int64_t N, int64_t K) {
   EpiArgs ea;
-  ea.out = nullptr; ea.ldo = 0; ea.out_dt = APA_DT_F32; ea.vec_out = 0; ea.tma_out = 0;
+  ea.out = nullptr; ea.ldo = 0; ea.out_dt = APA_DT_F32; ea.vec_out = 0; ea.tma_out = 0; ea.coalesced_out = 0;
   ea.bias = nullptr; ea.amax = nullptr; ea.flag = nullptr;
   ea.counters = nullptr; ea.ratio_max = nullptr; ea.vmin = 0.0f; ea.accumulate = 0;
   ea.M = (int)M; ea.N = (int)N; ea.K = (int)K;

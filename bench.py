@@ -585,7 +585,19 @@ def profile_case(case: str):
     dev = torch.device("cuda", 0)
     st = _lib.stream_handle(dev)
     g = torch.Generator(device=dev).manual_seed(0)
-    if case.startswith("gemm"):
+    if case == "gemm-fp8-k1024":
+        # an epilogue-bound FP8 forward: GPT-2-medium attention QKV projection
+        # (8192 tokens, 1024 -> 3072), fp32 output with telemetry
+        Mq, Kq, Nq = 8192, 1024, 3072
+        x = torch.randn(Mq, Kq, device=dev, generator=g).to(torch.float8_e4m3fn)
+        w = (torch.randn(Nq, Kq, device=dev, generator=g) * 0.02).to(torch.float8_e4m3fn)
+        y = torch.empty(Mq, Nq, device=dev)
+        amax = torch.zeros(1, device=dev)
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        for _ in range(3):
+            _lib.check(lib.apa_linear_fwd(0, x.data_ptr(), Kq, w.data_ptr(), Kq, None, y.data_ptr(), Nq, Mq, Nq, Kq,
+                                          amax.data_ptr(), flag.data_ptr(), st), "fwd")
+    elif case.startswith("gemm"):
         rung = {"gemm-fp8": 0, "gemm-fp16": 1, "gemm-tf32": 2}[case]
         dt = {0: torch.float8_e4m3fn, 1: torch.float16, 2: torch.float32}[rung]
         x = torch.randn(M, K, device=dev, generator=g).to(dt)
@@ -693,7 +705,8 @@ def main():
     ap.add_argument("--gpt-steps", type=int, default=10)
     ap.add_argument("--gpt-eager", action="store_true", help="time the GPT workloads without CUDA-graph replay")
     ap.add_argument("--profile-case", default=None,
-                    help="run a few launches of one kernel for an ncu capture (gemm-fp8|gemm-fp16|gemm-tf32|cast|dyprep), "
+                    help="run a few launches of one kernel for an ncu capture (gemm-fp8|gemm-fp16|gemm-tf32|gemm-fp8-k1024|cast|"
+                         "dyprep), "
                          "or one profiled step (step-fp8|step-fp16|step-tf32|step-gpt2m|step-gpt-char)")
     args = ap.parse_args()
     if args.profile_case:
