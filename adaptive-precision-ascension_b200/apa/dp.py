@@ -138,14 +138,22 @@ class GradientAverager:
             self._limit_gemms(False)
             self.limited = False
 
-    def finish(self):
-        """Issue every bucket not yet issued (in order) and make the current
-        stream wait for all of them; average when the backend has no AVG."""
+    def issue_remaining(self):
+        """Issue every bucket not yet issued, in order (asynchronous)."""
         if self.graphed:
             return
         while self.next < len(self.buckets):
             self._launch(self.buckets[self.next])
             self.next += 1
+
+    def finish(self):
+        """Issue every bucket not yet issued (in order) and make the current
+        stream wait for all of them; average when the backend has no AVG.
+        Nothing blocks the host: later work on the current stream (the
+        optimizer step) runs after the reductions."""
+        if self.graphed:
+            return
+        self.issue_remaining()
         for b in self.buckets:
             if b.handle is not None:
                 b.handle.wait()

@@ -104,6 +104,7 @@ class APAManager:
             self._register_forensic_forward_hooks()
         self._ladder: Optional[_LadderState] = None
         self._pg = process_group
+        self._telem_pg = None          # second communicator for the small telemetry reduction
         self._sync_gradients = sync_gradients
         self._bucket_bytes = bucket_bytes
         self._dp = None
@@ -229,24 +230,45 @@ class APAManager:
                 st.ema[: st.L].copy_(torch.tensor(emas, dtype=torch.float64))
             st.host_level, st.host_ema = levels, emas
 
-    def _run_ladder(self) -> dict:
+    def _telemetry_group(self):
+        """The telemetry MAX reduction runs on its own communicator so it does
+        not queue behind the gradient buckets still in flight on the main one
+        (collectives of one communicator run in issue order)."""
+        if self._telem_pg is None:
+            dist = torch.distributed
+            ranks = dist.get_process_group_ranks(self._pg) if self._pg is not None else list(
+                range(dist.get_world_size()))
+            self._telem_pg = dist.new_group(ranks=ranks, use_local_synchronization=True)
+        return self._telem_pg
+
+    def _run_ladder(self, before_wait=None) -> dict:
+        """One ladder evaluation. before_wait() (if given) is called once the
+        decision record's device-to-host copy is queued and before the host
+        waits for it: work it queues on the stream does not delay the record."""
         st = self._state()
         self._upload_ladder(st)
         lib = _lib.lib()
-        s = _lib.stream_handle(self._global_nonfinite.device)
+        dev = self._global_nonfinite.device
+        s = _lib.stream_handle(dev)
         glob = None
         if self._world() > 1:
             _lib.check(lib.apa_ladder_pack(st.L, st.amax.data_ptr(), st.ratio.data_ptr(), st.flag.data_ptr(), st.O,
                                            st.oamax.data_ptr(), st.oflag.data_ptr(), st.packed.data_ptr(), s),
                        "apa_ladder_pack")
-            torch.distributed.all_reduce(st.packed, op=torch.distributed.ReduceOp.MAX, group=self._pg)
+            torch.distributed.all_reduce(st.packed, op=torch.distributed.ReduceOp.MAX, group=self._telemetry_group())
             glob = st.packed.data_ptr()
         _lib.check(lib.apa_ladder_eval(st.L, st.amax.data_ptr(), st.ratio.data_ptr(), st.flag.data_ptr(),
                                        st.level.data_ptr(), st.ema.data_ptr(), st.O, st.oamax.data_ptr(),
                                        st.oflag.data_ptr(), glob, self.step_count, self.config.check_interval,
                                        float(self.config.theta_underflow), float(self.config.ema_alpha),
                                        st.out.data_ptr(), st.out_host.data_ptr(), s), "apa_ladder_eval")
-        torch.cuda.current_stream(self._global_nonfinite.device).synchronize()
+        if before_wait is None:
+            torch.cuda.current_stream(dev).synchronize()
+        else:
+            done = torch.cuda.Event()
+            done.record(torch.cuda.current_stream(dev))
+            before_wait()
+            done.synchronize()
         rec = st.parse()
         if rec["status"] & 1:
             lv = [int(v) for v in rec["level"]]
@@ -369,9 +391,15 @@ class APAManager:
     def post_backward_sync_and_eval(self) -> bool:
         self.step_count += 1
         self._sync_grads_to_master()
+        join = None
         if self._sync_gradients and self._world() > 1:
-            self._allreduce_grads()
-        rec = self._run_ladder()
+            # the remaining gradient buckets go out now; the stream joins them
+            # after the ladder's record copy, so the decision does not wait
+            # for the bulk reduction (the optimizer step, queued later, does)
+            avg = self._averager()
+            avg.issue_remaining()
+            join = avg.finish
+        rec = self._run_ladder(before_wait=join)
         self._log_record(rec)
         return not (rec["status"] & 2)
 

@@ -1,0 +1,107 @@
+"""Data parallel on 2+ GPUs (skipped with fewer): ranks that see different
+data take identical decisions.
+
+Each rank trains the same small model on its own batches; at one step only
+rank 1's batch carries an overflow spike. The reference evaluates local
+telemetry only (manager.py:221-256), so its ranks would disagree; here the
+telemetry is MAX-reduced before the ladder and the gradients are averaged, so
+every rank must skip that step, escalate the same layers, and keep
+bit-identical weights. NVLS is disabled so a rank that fails an assertion
+cannot leave a multicast binding behind."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+STEPS = 8
+SPIKE_STEP = 3
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import sys
+    from datetime import timedelta
+    import torch.distributed as dist
+    import torch.nn as nn
+    import torch.nn.functional as F
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                                    "adaptive-precision-ascension_b200"))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        from apa import APAConfig, APALinear, APAManager
+        class LayerNorm32(nn.LayerNorm):   # takes the fp16 output of an escalated layer
+            def forward(self, x):
+                return F.layer_norm(x.float(), self.normalized_shape, self.weight, self.bias, self.eps)
+
+        cfg = APAConfig(device=str(dev), check_interval=2)
+        torch.manual_seed(0)
+        model = nn.Sequential(APALinear(256, 256, config=cfg), nn.ReLU(), LayerNorm32(256),
+                              APALinear(256, 16, config=cfg)).to(dev)
+        mgr = APAManager(model, cfg)
+        opt = torch.optim.AdamW(mgr.get_trainable_parameters(), lr=1e-3)
+        g = torch.Generator().manual_seed(100 + rank)
+        keeps, levels = [], []
+        for step in range(STEPS):
+            x = torch.randn(128, 256, generator=g)
+            y = torch.randint(0, 16, (128,), generator=g)
+            if step == SPIKE_STEP and rank == 1:
+                idx = torch.randperm(x.numel(), generator=g)[:64]
+                x.view(-1)[idx] *= 1e3
+            x, y = x.to(dev), y.to(dev)
+            mgr.pre_step()
+            opt.zero_grad(set_to_none=True)
+            F.cross_entropy(model(x), y).backward()
+            keep = mgr.post_backward_sync_and_eval()
+            if keep:
+                opt.step()
+            keeps.append(bool(keep))
+            levels.append([m.level for m in mgr.apa_modules.values()])
+        torch.cuda.synchronize()
+        weights = [p.detach().double().cpu() for p in mgr.get_trainable_parameters()]
+        q.put((rank, keeps, levels, [w.sum().item() for w in weights], [w.abs().sum().item() for w in weights]))
+    except Exception as e:   # report, then leave the group normally
+        q.put((rank, "error", repr(e), None, None))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ranks_take_identical_decisions():
+    import torch.multiprocessing as mp
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = dict((r[0], r[1:]) for r in (q.get(timeout=300) for _ in procs))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(world):
+        assert out[r][0] != "error", out[r]
+    keeps0, levels0, sums0, abs0 = out[0]
+    for r in range(1, world):
+        keeps, levels, sums, abss = out[r]
+        assert keeps == keeps0
+        assert levels == levels0
+        assert sums == sums0 and abss == abs0     # bit-identical replicas
+    assert keeps0[SPIKE_STEP] is False            # only rank 1 saw the spike; every rank skips
+    assert all(keeps0[s] for s in range(STEPS) if s != SPIKE_STEP)
+    assert levels0[SPIKE_STEP][0] == 1            # the first layer escalated on every rank
