@@ -65,6 +65,8 @@ class GradientAverager:
         self.armed = False
         self.limited = False
         self.graphed = False
+        self.comm_stream = None        # forked stream for reductions captured in a CUDA graph
+        self.capture_fork = False
         apa_params = set()
         for m in mgr.apa_modules.values():
             m._grad_ready_cb = self._apa_ready
@@ -119,10 +121,28 @@ class GradientAverager:
         if not self.limited:
             self._limit_gemms(True)
             self.limited = True
-        if self.avg_op is not None:
-            b.handle = dist.all_reduce(b.flat, op=self.avg_op, group=self.pg, async_op=True)
+        op = self.avg_op if self.avg_op is not None else dist.ReduceOp.SUM
+        if b.flat.is_cuda and torch.cuda.is_current_stream_capturing():
+            # inside a CUDA-graph capture: the reduction runs on a stream forked
+            # from the capture stream, so the graph runs it alongside the
+            # kernels captured after it; join_capture() joins the fork at the end
+            cur = torch.cuda.current_stream(b.flat.device)
+            if self.comm_stream is None:
+                self.comm_stream = torch.cuda.Stream(device=b.flat.device)
+            self.comm_stream.wait_stream(cur)
+            with torch.cuda.stream(self.comm_stream):
+                dist.all_reduce(b.flat, op=op, group=self.pg)
+            self.capture_fork = True
+            b.handle = None
         else:
-            b.handle = dist.all_reduce(b.flat, op=dist.ReduceOp.SUM, group=self.pg, async_op=True)
+            b.handle = dist.all_reduce(b.flat, op=op, group=self.pg, async_op=True)
+
+    def join_capture(self, stream):
+        """End of a graph capture: the capture stream waits for the forked
+        reductions (they must rejoin before the capture ends)."""
+        if self.capture_fork:
+            stream.wait_stream(self.comm_stream)
+            self.capture_fork = False
 
     def _launch_ready(self):
         while self.next < len(self.buckets) and self.buckets[self.next].pending <= 0:

@@ -157,17 +157,28 @@ def run_ours(args):
     launches = 0
     clocks = None
     pk = peaks()
+    gstep = None
+    from apa.graphs import GraphedTrainStep
     for level, name in ((0, "fp8"), (1, "fp16"), (2, "tf32")):
         lin, mgr = make(level)
         dy = dy16 if level == 1 else dy32
         xr = x.detach().requires_grad_(True)
 
-        def step():
-            mgr.pre_step()
-            y = lin(xr)
-            y.backward(dy)
-            xr.grad = None
-            return mgr.post_backward_sync_and_eval()
+        if args.eager:
+            def step():
+                mgr.pre_step()
+                y = lin(xr)
+                y.backward(dy)
+                xr.grad = None
+                return mgr.post_backward_sync_and_eval()
+        else:
+            # pre_step + forward + backward replayed from a CUDA graph (the
+            # inputs stay in place), ladder decision eager: every step runs
+            # the same kernels as the eager path, minus the host launch work
+            gstep = GraphedTrainStep(mgr, lambda xx, gg: (lin(xx), gg), (xr, dy), warmup=2, static_inputs=True)
+
+            def step():
+                return gstep(xr, dy)[1]
 
         # the clock sampler starts before the warm-up (its process start-up
         # stays out of the timed region) and runs through the timed steps
@@ -190,11 +201,15 @@ def run_ours(args):
             clocks = sampler.summary()
         ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
         if level == 0:
-            launches = (_lib.calls - c0)
+            # library launches in the timed steps: the ones issued from the host
+            # plus those inside each replayed graph
+            launches = (_lib.calls - c0) + (0 if args.eager else args.steps * gstep.captured_launches)
         results[name] = {"ms_per_step": ms, "tflops": world * FLOPS_STEP / ms / 1e9,
                          "frac_of_peak": FLOPS_STEP / ms / 1e9 / pk[f"{name}_tflops"]}
         if level == 0:
             gemm_roof = time_gemm(torch, _lib, lin, xr, dev, pk)
+        # graphs holding NCCL work must be released before the process group
+        gstep = step = None
         del lin, mgr
         torch.cuda.empty_cache()
 
@@ -213,7 +228,9 @@ def run_ours(args):
             "metric": METRIC, "value": round(fp8["tflops"], 2), "unit": "TFLOP/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(fp8["ms_per_step"], 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3",
-            "data": "synthetic", "config": dict(CONFIG, parallelism=f"dp{world}"),
+            "data": "synthetic", "config": dict(CONFIG, parallelism=f"dp{world}",
+                                                launch="eager" if args.eager else
+                                                "cuda-graph replay of pre_step+fwd+bwd, ladder eager"),
             "rungs": {k: {"tflops": round(v["tflops"], 2), "ms_per_step": round(v["ms_per_step"], 4),
                           "frac_of_peak": round(v["frac_of_peak"], 4)} for k, v in results.items()},
             "roofline": gemm_roof,
@@ -712,6 +729,8 @@ def main():
                     help="GPT training workloads also timed (tokens/s), comma-separated; '' for none")
     ap.add_argument("--gpt-steps", type=int, default=10)
     ap.add_argument("--gpt-eager", action="store_true", help="time the GPT workloads without CUDA-graph replay")
+    ap.add_argument("--eager", action="store_true",
+                    help="time the APALinear steps without CUDA-graph replay (every launch from the host)")
     ap.add_argument("--profile-case", default=None,
                     help="run a few launches of one kernel for an ncu capture (gemm-fp8|gemm-fp16|gemm-tf32|gemm-fp8-k1024|cast|"
                          "dyprep), "

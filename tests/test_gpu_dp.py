@@ -28,7 +28,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, graphed):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -56,22 +56,34 @@ def _worker(rank, world, port, q):
         opt = torch.optim.AdamW(mgr.get_trainable_parameters(), lr=1e-3)
         g = torch.Generator().manual_seed(100 + rank)
         keeps, levels = [], []
+        xs = torch.empty(128, 256, device=dev)
+        ys = torch.empty(128, dtype=torch.long, device=dev)
+        gstep = None
+        if graphed:
+            from apa.graphs import GraphedTrainStep
+            gstep = GraphedTrainStep(mgr, lambda a, b: F.cross_entropy(model(a), b), (xs, ys), warmup=2,
+                                     static_inputs=True)
         for step in range(STEPS):
             x = torch.randn(128, 256, generator=g)
             y = torch.randint(0, 16, (128,), generator=g)
             if step == SPIKE_STEP and rank == 1:
                 idx = torch.randperm(x.numel(), generator=g)[:64]
                 x.view(-1)[idx] *= 1e3
-            x, y = x.to(dev), y.to(dev)
-            mgr.pre_step()
-            opt.zero_grad(set_to_none=True)
-            F.cross_entropy(model(x), y).backward()
-            keep = mgr.post_backward_sync_and_eval()
+            xs.copy_(x)
+            ys.copy_(y)
+            if gstep is not None:
+                _, keep = gstep(xs, ys)
+            else:
+                mgr.pre_step()
+                opt.zero_grad(set_to_none=True)
+                F.cross_entropy(model(xs), ys).backward()
+                keep = mgr.post_backward_sync_and_eval()
             if keep:
                 opt.step()
             keeps.append(bool(keep))
             levels.append([m.level for m in mgr.apa_modules.values()])
         torch.cuda.synchronize()
+        gstep = None   # a graph holding NCCL work is released before the group
         weights = [p.detach().double().cpu() for p in mgr.get_trainable_parameters()]
         q.put((rank, keeps, levels, [w.sum().item() for w in weights], [w.abs().sum().item() for w in weights]))
     except Exception as e:   # report, then leave the group normally
@@ -81,13 +93,16 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ranks_take_identical_decisions():
+@pytest.mark.parametrize("graphed", [False, True])
+def test_ranks_take_identical_decisions(graphed):
+    """graphed: the step replayed from a CUDA graph (reductions captured on a
+    forked stream, ladder gated on the step's compute)."""
     import torch.multiprocessing as mp
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, graphed)) for r in range(world)]
     for p in procs:
         p.start()
     out = dict((r[0], r[1:]) for r in (q.get(timeout=300) for _ in procs))
