@@ -3,8 +3,9 @@
 //
 // Same results as cast_kernel (every code, the telemetry pair, the per-64-row
 // column partial sums) for the layouts the hot path uses: an fp32 / bf16 /
-// fp16 source cast to E4M3 or fp16, 16-byte aligned rows everywhere, with a
-// row-major copy and/or a transposed copy. A persistent CTA per SM slot runs
+// fp16 source cast to E4M3, fp16 or fp32 (TF32-rounded at the TF32 rung),
+// 16-byte aligned rows everywhere, with a row-major copy and/or a transposed
+// copy. A persistent CTA per SM slot runs
 //   warp 4      one thread streams 64 x 128 source tiles into a ring of
 //               shared-memory stages with cp.async.bulk.tensor (128-byte
 //               swizzle, zero fill past the edges), mbarrier full/empty pairs
@@ -34,14 +35,16 @@ constexpr int kCastSmemBudget = 112 * 1024;   // two CTAs per SM
 
 template <int SRC, int DST> struct TcCfg {
   static constexpr int ES = SRC == APA_DT_F32 ? 4 : 2;
-  static constexpr int ED = DST == APA_DT_E4M3 ? 1 : 2;
+  static constexpr int ED = DST == APA_DT_E4M3 ? 1 : DST == APA_DT_F16 ? 2 : 4;
+  // fp32 destinations stage 64 KB per tile: one CTA per SM with a deeper ring
+  static constexpr int kBudget = ED == 4 ? 200 * 1024 : kCastSmemBudget;
   static constexpr int kStageBytes = kCTR * kCTC * ES;         // 16 / 32 KB
   static constexpr int kBoxCols = 128 / ES;                    // 128-byte swizzle boxes
   static constexpr int kBoxes = kCTC / kBoxCols;
   static constexpr int kOutBytes = kCTR * kCTC * ED;           // one staging tile
   static constexpr int kCsumBytes = 8 * kCTC * 4;
   static constexpr int kFixed = 2 * kOutBytes + kCsumBytes + 128;
-  static constexpr int kStagesFit = (kCastSmemBudget - 1024 - kFixed) / kStageBytes;
+  static constexpr int kStagesFit = (kBudget - 1024 - kFixed) / kStageBytes;
   static constexpr int kStages = kStagesFit > 4 ? 4 : (kStagesFit < 1 ? 1 : kStagesFit);
   static constexpr int kSmemBytes = kStages * kStageBytes + kFixed + 1024;
 };
@@ -136,10 +139,11 @@ struct TmaCastArgs {
   float* colsum;
   int telem_on_source;
   int has_dst, has_dst_t;
+  int tf32;                 // fp32 destination: stored values rounded to the TF32 grid
 };
 
 template <int SRC, int DST>
-__global__ void __launch_bounds__(kCastTmaThreads, 2)
+__global__ void __launch_bounds__(kCastTmaThreads, DST == APA_DT_F32 ? 1 : 2)
     cast_tma_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmD,
                     const __grid_constant__ CUtensorMap tmT, TmaCastArgs p) {
   using C = TcCfg<SRC, DST>;
@@ -258,10 +262,12 @@ __global__ void __launch_bounds__(kCastTmaThreads, 2)
         for (int c = 0; c < 8; ++c) m = max(m, mag_bits(v[r][c]));
       msrc = max(msrc, m);
 
-      // ---- encode; code words per row: E4M3 2 words, fp16 4 words ----
-      constexpr int W = C::ED * 2;
+      // ---- encode; code words per row: E4M3 2 words, fp16 4 words (fp32
+      // values are stored from v, rounded to TF32 on the way out if asked) ----
+      constexpr int W = C::ED == 4 ? 1 : C::ED * 2;
       uint32_t code[8][W];
-      if constexpr (DST == APA_DT_E4M3) {
+      if constexpr (DST == APA_DT_F32) {
+      } else if constexpr (DST == APA_DT_E4M3) {
         const bool big = m > kE4M3NaNThresholdBits;
 #pragma unroll
         for (int r = 0; r < 8; ++r)
@@ -299,7 +305,10 @@ __global__ void __launch_bounds__(kCastTmaThreads, 2)
         for (int c = 0; c < 8; ++c) cs[c] = 0.0f;
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
-          if constexpr (DST == APA_DT_E4M3) {
+          if constexpr (DST == APA_DT_F32) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) cs[c] += v[r][c];
+          } else if constexpr (DST == APA_DT_E4M3) {
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const uint32_t h = f16x2_from_e4m3x2((code[r][k >> 1] >> (16 * (k & 1))) & 0xFFFFu);
@@ -345,7 +354,21 @@ __global__ void __launch_bounds__(kCastTmaThreads, 2)
 #pragma unroll
         for (int r = 0; r < 8; ++r) {
           const int R = 8 * bi + r;
-          if constexpr (DST == APA_DT_E4M3) {
+          if constexpr (DST == APA_DT_F32) {
+            // two 16-byte chunks (columns 0-3, 4-7 of the block) in 32-column
+            // boxes; the thread writes chunk f first (f = (j%8)/4)
+            uint32_t w[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) w[c] = p.tf32 ? tf32_rn_bits(__float_as_uint(v[r][c])) : __float_as_uint(v[r][c]);
+            const int f = (bj & 7) >> 2;
+            uint8_t* rowp = sOut + (bj >> 2) * (kCTR * 128) + R * 128;
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+              const int k = kk ^ f;
+              const uint4 val = k ? make_uint4(w[4], w[5], w[6], w[7]) : make_uint4(w[0], w[1], w[2], w[3]);
+              *reinterpret_cast<uint4*>(rowp + (((2 * (bj & 3) + k) ^ r) << 4)) = val;
+            }
+          } else if constexpr (DST == APA_DT_E4M3) {
             *reinterpret_cast<uint2*>(sOut + R * 128 + (((bj >> 1) ^ r) << 4) + ((bj & 1) << 3)) =
                 make_uint2(code[r][0], code[r][1]);
           } else {
@@ -359,7 +382,24 @@ __global__ void __launch_bounds__(kCastTmaThreads, 2)
         for (int c = 0; c < 8; ++c) {
           const int cc = c ^ gflip;
           const int R = 8 * bj + cc;
-          if constexpr (DST == APA_DT_E4M3) {
+          if constexpr (DST == APA_DT_F32) {
+            // column cc over the block's 8 rows: chunks rows 0-3 / 4-7 in the
+            // 32-row boxes of the transposed tile; chunk i/4 first
+            uint32_t w[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const float e = gflip ? v[k][c ^ 1] : v[k][c];
+              w[k] = p.tf32 ? tf32_rn_bits(__float_as_uint(e)) : __float_as_uint(e);
+            }
+            const int f = bi >> 2;
+            uint8_t* rowp = sOutT + (bi >> 2) * (kCTC * 128) + R * 128;
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+              const int k = kk ^ f;
+              const uint4 val = k ? make_uint4(w[4], w[5], w[6], w[7]) : make_uint4(w[0], w[1], w[2], w[3]);
+              *reinterpret_cast<uint4*>(rowp + (((2 * (bi & 3) + k) ^ (R & 7)) << 4)) = val;
+            }
+          } else if constexpr (DST == APA_DT_E4M3) {
             const uint32_t w0 = gflip ? T[c ^ 1][0] : T[c][0];
             const uint32_t w1 = gflip ? T[c ^ 1][1] : T[c][1];
             *reinterpret_cast<uint2*>(sOutT + R * 64 + (((bi >> 1) ^ ((R >> 1) & 3)) << 4) + ((bi & 1) << 3)) =
@@ -386,12 +426,23 @@ __global__ void __launch_bounds__(kCastTmaThreads, 2)
         if (p.has_dst) {
           if constexpr (DST == APA_DT_E4M3) {
             ct_store(&tmD, sOut, x, y);
-          } else {
+          } else if constexpr (DST == APA_DT_F16) {
             ct_store(&tmD, sOut, x, y);
             if (x + 64 < p.cols) ct_store(&tmD, sOut + kCTR * 128, x + 64, y);
+          } else {
+#pragma unroll
+            for (int b = 0; b < 4; ++b)
+              if (x + 32 * b < p.cols) ct_store(&tmD, sOut + b * (kCTR * 128), x + 32 * b, y);
           }
         }
-        if (p.has_dst_t) ct_store(&tmT, sOutT, y, x);
+        if (p.has_dst_t) {
+          if constexpr (DST == APA_DT_F32) {
+            ct_store(&tmT, sOutT, y, x);
+            if (y + 32 < p.rows) ct_store(&tmT, sOutT + kCTC * 128, y + 32, x);
+          } else {
+            ct_store(&tmT, sOutT, y, x);
+          }
+        }
         ct_commit();
       }
       if (p.colsum) {
@@ -410,7 +461,7 @@ __global__ void __launch_bounds__(kCastTmaThreads, 2)
   uint32_t mag = msrc;
   if (!p.telem_on_source) {
     if constexpr (DST == APA_DT_E4M3) mag = e4m3_mag_bits(e4m3_from_f32(__uint_as_float(msrc)));
-    else mag = mag_bits(f16_to_f32(f16_from_f32(__uint_as_float(msrc))));
+    else if constexpr (DST == APA_DT_F16) mag = mag_bits(f16_to_f32(f16_from_f32(__uint_as_float(msrc))));
   }
   mag = warp_max_u32(mag);
   if (lane == 0) red[warp] = mag;
@@ -459,7 +510,9 @@ int launch_cast_tma_t(const CastParams& cp, cudaStream_t s) {
   const CUtensorMapDataType sdt = SRC == APA_DT_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                   : SRC == APA_DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const CUtensorMapDataType ddt = DST == APA_DT_E4M3 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType ddt = DST == APA_DT_E4M3  ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                  : DST == APA_DT_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
   CUtensorMap ms, md, mt;
   if (!cast_map(&ms, sdt, cp.src, cp.cols, cp.rows, cp.ld_src * C::ES, C::kBoxCols, kCTR,
                 CU_TENSOR_MAP_SWIZZLE_128B))
@@ -467,13 +520,14 @@ int launch_cast_tma_t(const CastParams& cp, cudaStream_t s) {
   md = ms;
   mt = ms;
   if (cp.dst) {
-    const int bx = DST == APA_DT_E4M3 ? 128 : 64;
+    const int bx = 128 / C::ED;
     if (!cast_map(&md, ddt, cp.dst, cp.cols, cp.rows, cp.ld_dst * C::ED, bx, kCTR, CU_TENSOR_MAP_SWIZZLE_128B))
       return APA_ERR_UNSUPPORTED;
   }
   if (cp.dst_t) {
     const CUtensorMapSwizzle sw = DST == APA_DT_E4M3 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
-    if (!cast_map(&mt, ddt, cp.dst_t, cp.rows, cp.cols, cp.ld_dst_t * C::ED, kCTR, kCTC, sw))
+    const int bx = DST == APA_DT_F32 ? 32 : kCTR;
+    if (!cast_map(&mt, ddt, cp.dst_t, cp.rows, cp.cols, cp.ld_dst_t * C::ED, bx, kCTC, sw))
       return APA_ERR_UNSUPPORTED;
   }
   TmaCastArgs a;
@@ -481,6 +535,7 @@ int launch_cast_tma_t(const CastParams& cp, cudaStream_t s) {
   a.amax = cp.amax; a.flag = cp.flag; a.merge_amax = cp.merge_amax;
   a.colsum = cp.colsum; a.telem_on_source = cp.telem_on_source;
   a.has_dst = cp.dst != nullptr; a.has_dst_t = cp.dst_t != nullptr;
+  a.tf32 = cp.tf32;
   const int64_t tiles = ((cp.rows + kCTR - 1) / kCTR) * ((cp.cols + kCTC - 1) / kCTC);
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)num_sms() * blocks_per_sm));
   cast_tma_kernel<SRC, DST><<<(unsigned)grid, kCastTmaThreads, C::kSmemBytes, s>>>(ms, md, mt, a);
@@ -493,16 +548,15 @@ bool tma_ok(const void* p, int64_t ld, int es) {
 
 }  // namespace
 
-// The streaming kernel when it applies (E4M3 / fp16 destination, at least one
+// The streaming kernel when it applies (E4M3 / fp16 / fp32 destination, at least one
 // output copy, 16-byte aligned rows, sizes a tensor map can describe);
 // APA_ERR_UNSUPPORTED otherwise, and the caller uses cast_kernel.
 int cast_tma_try(int src_dt, int dst_dt, const CastParams& p, cudaStream_t s) {
-  if (p.tf32) return APA_ERR_UNSUPPORTED;
-  if (dst_dt != APA_DT_E4M3 && dst_dt != APA_DT_F16) return APA_ERR_UNSUPPORTED;
+  if (dst_dt != APA_DT_E4M3 && dst_dt != APA_DT_F16 && dst_dt != APA_DT_F32) return APA_ERR_UNSUPPORTED;
   if (src_dt != APA_DT_F32 && src_dt != APA_DT_BF16 && src_dt != APA_DT_F16) return APA_ERR_UNSUPPORTED;
   if (!p.dst && !p.dst_t) return APA_ERR_UNSUPPORTED;
   if (p.rows <= 0 || p.cols <= 0 || p.rows >= (1ll << 31) || p.cols >= (1ll << 31)) return APA_ERR_UNSUPPORTED;
-  const int es = src_dt == APA_DT_F32 ? 4 : 2, ed = dst_dt == APA_DT_E4M3 ? 1 : 2;
+  const int es = src_dt == APA_DT_F32 ? 4 : 2, ed = dst_dt == APA_DT_E4M3 ? 1 : dst_dt == APA_DT_F16 ? 2 : 4;
   if (!tma_ok(p.src, p.ld_src, es)) return APA_ERR_UNSUPPORTED;
   if (p.dst && !tma_ok(p.dst, p.ld_dst, ed)) return APA_ERR_UNSUPPORTED;
   if (p.dst_t && !tma_ok(p.dst_t, p.ld_dst_t, ed)) return APA_ERR_UNSUPPORTED;
@@ -514,6 +568,9 @@ int cast_tma_try(int src_dt, int dst_dt, const CastParams& p, cudaStream_t s) {
   APA_TC(APA_DT_F32, APA_DT_F16)
   APA_TC(APA_DT_BF16, APA_DT_F16)
   APA_TC(APA_DT_F16, APA_DT_F16)
+  APA_TC(APA_DT_F32, APA_DT_F32)
+  APA_TC(APA_DT_BF16, APA_DT_F32)
+  APA_TC(APA_DT_F16, APA_DT_F32)
 #undef APA_TC
   return APA_ERR_UNSUPPORTED;
 }

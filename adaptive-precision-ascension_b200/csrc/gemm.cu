@@ -111,6 +111,7 @@ struct EpiArgs {
   float* ratio_max;                 // WGRAD: module gpu_underflow_ratio
   float vmin;                       // WGRAD: underflow threshold as fp32
   int accumulate;                   // WGRAD: add into out instead of overwriting
+  int telem;                        // 0: no telemetry buffers, skip the telemetry-only work
   int M, N, K;
 };
 
@@ -381,14 +382,15 @@ __device__ __forceinline__ void epi_unit(const EpiArgs& ea, const float* sb, uin
         r[4 * q + 3] = __float_as_uint(fu(r[4 * q + 3]) + b.w);
       }
     }
-    st.mag = max(st.mag, chunk_max(r, 64, check, row_ok, nv));
+    if (ea.telem) st.mag = max(st.mag, chunk_max(r, 64, check, row_ok, nv));
     if constexpr (KIND == KIND_F16) {
 #pragma unroll
       for (int k = 0; k < 32; ++k) r[k] = f16x2_from_f32(fu(r[2 * k]), fu(r[2 * k + 1]));
     }
   } else if constexpr (EPI == EPI_DGRAD) {
-    const uint32_t m = chunk_max(r, 64, check, row_ok, nv);
-    st.mag = max(st.mag, m);
+    // the chunk max also selects the E4M3 conversion (NaN rule above 464)
+    const uint32_t m = (KIND == KIND_E4M3 || ea.telem) ? chunk_max(r, 64, check, row_ok, nv) : 0u;
+    if (ea.telem) st.mag = max(st.mag, m);
     const int od = ea.out_dt;
     if constexpr (KIND == KIND_E4M3) {
       const bool big = __any_sync(0xFFFFFFFFu, m > kE4M3NaNThresholdBits);
@@ -434,13 +436,15 @@ __device__ __forceinline__ void epi_unit(const EpiArgs& ea, const float* sb, uin
     const uint32_t vb = __float_as_uint(ea.vmin);
     if constexpr (KIND == KIND_E4M3) {
       const uint32_t m = chunk_max(r, 64, check, row_ok, nv);
+      if (ea.telem) {
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        // nonzero: 0 < |v| <= Inf (NaN excluded); underflow: nonzero and |v| < vmin
-        const uint32_t a = (r[j] & 0x7FFFFFFFu) - 1u;
-        const bool ok = !check || (row_ok && j < nv);
-        st.nz += (ok && a < 0x7F800000u) ? 1u : 0u;
-        st.uf += (ok && a < vb - 1u) ? 1u : 0u;
+        for (int j = 0; j < 64; ++j) {
+          // nonzero: 0 < |v| <= Inf (NaN excluded); underflow: nonzero and |v| < vmin
+          const uint32_t a = (r[j] & 0x7FFFFFFFu) - 1u;
+          const bool ok = !check || (row_ok && j < nv);
+          st.nz += (ok && a < 0x7F800000u) ? 1u : 0u;
+          st.uf += (ok && a < vb - 1u) ? 1u : 0u;
+        }
       }
       const bool big = __any_sync(0xFFFFFFFFu, m > kE4M3NaNThresholdBits);
 #pragma unroll
@@ -457,12 +461,14 @@ __device__ __forceinline__ void epi_unit(const EpiArgs& ea, const float* sb, uin
         r[2 * k] = __float_as_uint(f16lo_to_f32(h));
         r[2 * k + 1] = __float_as_uint(f16hi_to_f32(h));
       }
+      if (ea.telem) {
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        const uint32_t a = (r[j] & 0x7FFFFFFFu) - 1u;
-        const bool ok = !check || (row_ok && j < nv);
-        st.nz += (ok && a < 0x7F800000u) ? 1u : 0u;
-        st.uf += (ok && a < vb - 1u) ? 1u : 0u;
+        for (int j = 0; j < 64; ++j) {
+          const uint32_t a = (r[j] & 0x7FFFFFFFu) - 1u;
+          const bool ok = !check || (row_ok && j < nv);
+          st.nz += (ok && a < 0x7F800000u) ? 1u : 0u;
+          st.uf += (ok && a < vb - 1u) ? 1u : 0u;
+        }
       }
     }
   }
@@ -1173,7 +1179,7 @@ EpiArgs blank(int64_t M, int64_t N, int64_t K) {
   EpiArgs ea;
   ea.out = nullptr; ea.ldo = 0; ea.out_dt = APA_DT_F32; ea.vec_out = 0; ea.tma_out = 0; ea.coalesced_out = 0;
   ea.bias = nullptr; ea.amax = nullptr; ea.flag = nullptr;
-  ea.counters = nullptr; ea.ratio_max = nullptr; ea.vmin = 0.0f; ea.accumulate = 0;
+  ea.counters = nullptr; ea.ratio_max = nullptr; ea.vmin = 0.0f; ea.accumulate = 0; ea.telem = 0;
   ea.M = (int)M; ea.N = (int)N; ea.K = (int)K;
   return ea;
 }
@@ -1194,6 +1200,7 @@ extern "C" int apa_linear_fwd(int rung, const void* xq, int64_t ldx, const void*
   ea.out_dt = rung == APA_RUNG_FP16 ? APA_DT_F16 : APA_DT_F32;
   ea.vec_out = out_vec(y, ldy, rung == APA_RUNG_FP16 ? 2 : 4);
   ea.bias = bias_q; ea.amax = amax; ea.flag = reinterpret_cast<int*>(flag);
+  ea.telem = (amax || flag) ? 1 : 0;
   return apa::gemm_dispatch(rung, apa::gemm::EPI_FWD, xq, ldx, wq, ldw, ea, 0, 0, static_cast<cudaStream_t>(stream));
 }
 
@@ -1208,6 +1215,7 @@ extern "C" int apa_linear_dgrad(int rung, const void* dyq, int64_t lddy, const v
   ea.out = dx; ea.ldo = lddx; ea.out_dt = dx_dtype;
   ea.vec_out = out_vec(dx, lddx, dx_dtype == APA_DT_F32 ? 4 : 2);
   ea.amax = bc_amax; ea.flag = reinterpret_cast<int*>(bc_flag);
+  ea.telem = (bc_amax || bc_flag) ? 1 : 0;
   return apa::gemm_dispatch(rung, apa::gemm::EPI_DGRAD, dyq, lddy, wqt, ldwt, ea, 0, 0,
                             static_cast<cudaStream_t>(stream));
 }
@@ -1223,6 +1231,7 @@ extern "C" int apa_linear_wgrad(int rung, const void* dyqt, int64_t lddyt, const
   EpiArgs ea = blank(N, K, M);
   ea.out = dw; ea.ldo = lddw; ea.out_dt = APA_DT_F32; ea.vec_out = out_vec(dw, lddw, 4);
   ea.accumulate = accumulate; ea.counters = counters; ea.ratio_max = ratio_max;
+  ea.telem = counters ? 1 : 0;
   ea.vmin = rung == APA_RUNG_FP8 ? 0.015625f : rung == APA_RUNG_FP16 ? 6.1035e-5f : 0.0f;
   return apa::gemm_dispatch(rung, apa::gemm::EPI_WGRAD, dyqt, lddyt, xqt, ldxt, ea, 0, 0,
                             static_cast<cudaStream_t>(stream));

@@ -428,7 +428,9 @@ def run_gpt(torch, dist, name, world, rank, dev, steps, warmup, barrier, max_ove
 
 def time_gemm(torch, _lib, lin, xr, dev, pk):
     """The dominant kernel: the FP8 tcgen05 GEMM (forward, 8192x4096x4096),
-    timed alone with CUDA events on its launching stream."""
+    timed alone with CUDA events on its launching stream. Also times the same
+    GEMM without bias twice, with the fused telemetry (amax / NaN flag of y)
+    and bare (apa_gemm_tn: no telemetry work at all), for the telemetry cost."""
     lib = _lib.lib()
     wq = lin._wq
     xq = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=dev)
@@ -440,20 +442,32 @@ def time_gemm(torch, _lib, lin, xr, dev, pk):
     s = torch.cuda.current_stream(dev)
     st = _lib.stream_handle(dev)
 
-    def launch():
-        _lib.check(lib.apa_linear_fwd(0, xq.data_ptr(), K, wq.data_ptr(), wq.stride(0), lin._bq.data_ptr(),
-                                      y.data_ptr(), N, M, N, K, amax.data_ptr(), flag.data_ptr(), st), "fwd")
+    def fused(bias):
+        _lib.check(lib.apa_linear_fwd(0, xq.data_ptr(), K, wq.data_ptr(), wq.stride(0), bias, y.data_ptr(), N, M, N,
+                                      K, amax.data_ptr(), flag.data_ptr(), st), "fwd")
 
-    for _ in range(5):
-        launch()
-    reps = 50
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    for _ in range(reps):
-        launch()
-    e1.record(s)
-    torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) / reps * 1e3
+    def bare():
+        _lib.check(lib.apa_gemm_tn(0, 0, xq.data_ptr(), K, wq.data_ptr(), wq.stride(0), y.data_ptr(), _lib.DT_F32, N,
+                                   M, N, K, 0, 0, st), "gemm_tn")
+
+    def timed(fn, reps=50):
+        for _ in range(5):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(reps):
+            fn()
+        e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps * 1e3
+
+    us = timed(lambda: fused(lin._bq.data_ptr()))
+    # alternate the two telemetry variants so clock drift affects both alike
+    t_tel, t_bare = [], []
+    for _ in range(3):
+        t_tel.append(timed(lambda: fused(None), 30))
+        t_bare.append(timed(bare, 30))
+    tel, bar = min(t_tel), min(t_bare)
     achieved = 2.0 * M * N * K / (us * 1e-6) / 1e12
     tile, ew = ctypes.c_int(0), ctypes.c_int(0)
     _lib.check(lib.apa_gemm_plan(0, 0, M, N, K, _lib.DT_F32, 0, 0, ctypes.addressof(tile), ctypes.addressof(ew)),
@@ -465,6 +479,9 @@ def time_gemm(torch, _lib, lin, xr, dev, pk):
             "frac": round(achieved / pk["fp8_tflops"], 4), "us_per_launch": round(us, 2),
             "peak_note": f"2 x {pk['source']} bf16 cuBLAS burst ({pk['bf16_tflops']} TFLOP/s); "
                          "spec dense FP8 4500 TFLOP/s",
+            "telemetry": {"us_with": round(tel, 2), "us_bare": round(bar, 2),
+                          "overhead": round(tel / bar - 1.0, 4),
+                          "note": "forward without bias: fused amax/NaN telemetry vs the same kernel with none"},
             # dram__bytes_read.sum + dram__bytes_write.sum of this kernel from one ncu
             # capture (profiles/gemm_fp8_fwd_8192x4096x4096.md), bytes per launch
             "traffic": 145.9e6}

@@ -1,5 +1,7 @@
 """The streaming (TMA) cast kernel, taken by apa_cast whenever the source and
-every destination row is 16-byte aligned and the destination is E4M3 or fp16.
+every destination row is 16-byte aligned and the destination is E4M3, fp16 or
+fp32 (TF32-rounded at the TF32 rung: stored values rounded, telemetry and
+column sums on the unrounded values).
 
 Bit-exact against the oracle: every code of the row-major and transposed
 copies, amax and the NaN/Inf flag (on the source or on the cast values); the
@@ -41,54 +43,65 @@ def make_source(shape, src_dt, special):
     return x.to(src_dt)
 
 
-def cast_bits(xf, dst_dt):
-    if dst_dt == torch.float8_e4m3fn:
+DST = {"e4m3": (torch.float8_e4m3fn, 3), "f16": (torch.float16, 1), "f32": (torch.float32, 0),
+       "tf32": (torch.float32, 4)}
+
+
+def cast_bits(xf, dst):
+    if dst == "e4m3":
         b = O.f32_to_e4m3_bits(xf)
         return b, O.e4m3_bits_to_f32(b)
-    b = O.f32_to_f16_bits(xf)
-    return b, O.f16_bits_to_f32(b)
+    if dst == "f16":
+        b = O.f32_to_f16_bits(xf)
+        return b, O.f16_bits_to_f32(b)
+    stored = O.tf32_rn(xf) if dst == "tf32" else xf
+    return np.ascontiguousarray(stored).view(np.uint32), xf
 
 
 def got_bits(t):
     if t.dtype == torch.float8_e4m3fn:
         return t.view(torch.uint8).cpu().numpy()
+    if t.dtype == torch.float32:
+        return t.view(torch.int32).cpu().numpy().view(np.uint32)
     return t.view(torch.int16).cpu().numpy().view(np.uint16)
 
 
-def same_codes(got, ref, dst_dt):
-    if dst_dt == torch.float8_e4m3fn:
+def same_codes(got, ref, dst):
+    if dst == "e4m3":
         return np.array_equal(got, ref)
-    gn = (got & 0x7FFF) > 0x7C00
-    rn = (ref & 0x7FFF) > 0x7C00
+    mag, inf, sign = (0x7FFF, 0x7C00, 0x8000) if dst == "f16" else (0x7FFFFFFF, 0x7F800000, 0x80000000)
+    gn = (got & mag) > inf
+    rn = (ref & mag) > inf
     return (np.array_equal(gn, rn) and np.array_equal(got[~gn], ref[~rn])
-            and np.array_equal(got[gn] & 0x8000, ref[rn] & 0x8000))
+            and np.array_equal(got[gn] & sign, ref[rn] & sign))
 
 
 @pytest.mark.parametrize("shape", SHAPES)
 @pytest.mark.parametrize("src_dt", [torch.float32, torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("dst_dt", [torch.float8_e4m3fn, torch.float16])
+@pytest.mark.parametrize("dst", list(DST))
 @pytest.mark.parametrize("special", [False, True])
-def test_streaming_cast_exact(L, shape, src_dt, dst_dt, special):
+def test_streaming_cast_exact(L, shape, src_dt, dst, special):
     rows, cols = shape
+    dst_dt, dst_code = DST[dst]
     x = make_source(shape, src_dt, special)
     xf = x.float().numpy()
-    ref_bits, q = cast_bits(xf, dst_dt)
+    ref_bits, q = cast_bits(xf, dst)
     xc = x.cuda()
     for mode in ("both", "row", "t"):
         for telem_src in (0, 1):
-            dst = torch.empty(rows, cols, dtype=dst_dt, device="cuda") if mode != "t" else None
-            dst_t = torch.empty(cols, rows, dtype=dst_dt, device="cuda") if mode != "row" else None
+            out = torch.empty(rows, cols, dtype=dst_dt, device="cuda") if mode != "t" else None
+            out_t = torch.empty(cols, rows, dtype=dst_dt, device="cuda") if mode != "row" else None
             amax = torch.zeros(1, device="cuda")
             flag = torch.zeros(1, dtype=torch.int32, device="cuda")
             part = torch.full(((rows + 63) // 64, cols), 5.0, device="cuda")
-            L.check(L.lib().apa_cast(xc.data_ptr(), L.dt_code(src_dt), rows, cols, cols, L.ptr(dst),
-                                     L.dt_code(dst_dt), cols, L.ptr(dst_t), rows, amax.data_ptr(), flag.data_ptr(),
+            L.check(L.lib().apa_cast(xc.data_ptr(), L.dt_code(src_dt), rows, cols, cols, L.ptr(out),
+                                     dst_code, cols, L.ptr(out_t), rows, amax.data_ptr(), flag.data_ptr(),
                                      telem_src, None, part.data_ptr(), L.stream_handle()), "apa_cast")
             torch.cuda.synchronize()
-            if dst is not None:
-                assert same_codes(got_bits(dst), ref_bits, dst_dt), (mode, telem_src)
-            if dst_t is not None:
-                assert same_codes(got_bits(dst_t), np.ascontiguousarray(ref_bits.T), dst_dt), (mode, telem_src)
+            if out is not None:
+                assert same_codes(got_bits(out), ref_bits, dst), (mode, telem_src)
+            if out_t is not None:
+                assert same_codes(got_bits(out_t), np.ascontiguousarray(ref_bits.T), dst), (mode, telem_src)
             ref_amax, ref_flag = O.track(0.0, 0, xf if telem_src else q)
             assert flag.item() == ref_flag
             a = amax.item()
