@@ -18,7 +18,7 @@ LIB_PATH = os.path.join(_HERE, "libapa_kernels.so")
 OK, ERR_INVALID, ERR_ALIGN, ERR_UNSUPPORTED, ERR_CUDA, ERR_NOALLOC_LIMIT = 0, 1, 2, 3, 4, 5
 DT_F32, DT_F16, DT_BF16, DT_E4M3, DT_TF32 = 0, 1, 2, 3, 4
 RUNG_FP8, RUNG_FP16, RUNG_TF32 = 0, 1, 2
-EPI_FWD, EPI_DGRAD, EPI_WGRAD = 0, 1, 2
+EPI_FWD, EPI_DGRAD, EPI_WGRAD, EPI_RAW = 0, 1, 2, 3
 
 _VP = ctypes.c_void_p
 _I64 = ctypes.c_int64
@@ -38,6 +38,8 @@ SIGNATURES = {
     "apa_linear_fwd": [_I, _VP, _I64, _VP, _I64, _VP, _VP, _I64, _I64, _I64, _I64, _VP, _VP, _VP],
     "apa_linear_dgrad": [_I, _VP, _I64, _VP, _I64, _VP, _I, _I64, _I64, _I64, _I64, _VP, _VP, _VP],
     "apa_linear_wgrad": [_I, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _I64, _I, _VP, _VP, _VP],
+    "apa_wgrad_workspace_bytes": [_I, _I64, _I64, _I64, _VP],
+    "apa_linear_wgrad_ws": [_I, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _I64, _I, _VP, _VP, _VP, _I64, _VP],
     "apa_set_gemm_sm_limit": [_I],
     "apa_gemm_tn": [_I, _I, _VP, _I64, _VP, _I64, _VP, _I, _I64, _I64, _I64, _I64, _I, _I, _VP],
     "apa_gemm_plan": [_I, _I, _I64, _I64, _I64, _I, _I, _I, _VP, _VP],

@@ -28,6 +28,8 @@ grad copy to the masters are all folded into those launches.
 """
 from __future__ import annotations
 
+import ctypes
+
 import math
 from typing import Optional
 
@@ -258,10 +260,23 @@ class _APALinearFn(torch.autograd.Function):
                 if g is None:
                     g = torch.empty_like(W)
                 accumulate = 0
-            st = lib.apa_linear_wgrad(level, dyqt.data_ptr(), dyqt.stride(0), ctx.xqt.data_ptr(), ctx.xqt.stride(0),
-                                      g.data_ptr(), K, M, N, K, accumulate, mod._uf_counters.data_ptr(),
-                                      mod.gpu_underflow_ratio.data_ptr(), s)
-            _lib.check(st, "apa_linear_wgrad")
+            # small weight gradients over long token counts are split along the
+            # tokens (two kernels, fp32 partial sums in a scratch buffer)
+            nbytes = ctypes.c_int64(0)
+            _lib.check(lib.apa_wgrad_workspace_bytes(level, M, N, K, ctypes.addressof(nbytes)),
+                       "apa_wgrad_workspace_bytes")
+            if nbytes.value > 0:
+                ws = torch.empty(nbytes.value, dtype=torch.uint8, device=g.device)
+                st = lib.apa_linear_wgrad_ws(level, dyqt.data_ptr(), dyqt.stride(0), ctx.xqt.data_ptr(),
+                                             ctx.xqt.stride(0), g.data_ptr(), K, M, N, K, accumulate,
+                                             mod._uf_counters.data_ptr(), mod.gpu_underflow_ratio.data_ptr(),
+                                             ws.data_ptr(), nbytes.value, s)
+                _lib.check(st, "apa_linear_wgrad_ws")
+            else:
+                st = lib.apa_linear_wgrad(level, dyqt.data_ptr(), dyqt.stride(0), ctx.xqt.data_ptr(),
+                                          ctx.xqt.stride(0), g.data_ptr(), K, M, N, K, accumulate,
+                                          mod._uf_counters.data_ptr(), mod.gpu_underflow_ratio.data_ptr(), s)
+                _lib.check(st, "apa_linear_wgrad")
             if W.grad is None:
                 W.grad = g
             if f_on:

@@ -67,7 +67,8 @@ template <int EW> constexpr int threads_for() { return 64 + 32 * EW; }
 
 
 enum { KIND_E4M3 = 0, KIND_F16 = 1, KIND_TF32 = 2 };
-enum { EPI_FWD = 0, EPI_DGRAD = 1, EPI_WGRAD = 2 };
+// EPI_RAW: the fp32 accumulator as is (split-K partial sums, bare timing)
+enum { EPI_FWD = 0, EPI_DGRAD = 1, EPI_WGRAD = 2, EPI_RAW = 3 };
 
 template <int KIND> struct KindInfo;
 template <> struct KindInfo<KIND_E4M3> { static constexpr int bytes = 1; static constexpr uint32_t fmt = 0; };
@@ -112,6 +113,9 @@ struct EpiArgs {
   float vmin;                       // WGRAD: underflow threshold as fp32
   int accumulate;                   // WGRAD: add into out instead of overwriting
   int telem;                        // 0: no telemetry buffers, skip the telemetry-only work
+  int splits;                       // split-K: K blocks divided into this many units per tile
+  int kb_per_split;                 // 128-byte K slabs per split
+  int split_rows;                   // output row offset between the splits' slices
   int M, N, K;
 };
 
@@ -432,6 +436,8 @@ __device__ __forceinline__ void epi_unit(const EpiArgs& ea, const float* sb, uin
         for (int k = 0; k < 32; ++k) r[k] = f16x2_from_f32(fu(r[2 * k]), fu(r[2 * k + 1]));
       }
     }
+  } else if constexpr (EPI == EPI_RAW) {
+    // raw fp32 accumulator: nothing to apply
   } else {
     const uint32_t vb = __float_as_uint(ea.vmin);
     if constexpr (KIND == KIND_E4M3) {
@@ -623,6 +629,9 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
   const int num_m = (ea.M + C::kTileM - 1) / C::kTileM;
   const int num_tiles = num_m * num_n;
   const int kb_count = (int)(((int64_t)ea.K * KindInfo<KIND>::bytes + kSlab - 1) / kSlab);
+  // work units: (tile, K split); one split covers the whole K range
+  const int splits = ea.splits > 1 ? ea.splits : 1;
+  const int num_units = num_tiles * splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -659,12 +668,15 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = unit0; ok && tile < num_tiles; tile += units) {
+      for (int w = unit0; ok && w < num_units; w += units) {
+        const int tile = w / splits, split = w - tile * splits;
+        const int kb0 = splits > 1 ? split * ea.kb_per_split : 0;
+        const int kb1 = splits > 1 ? min(kb0 + ea.kb_per_split, kb_count) : kb_count;
         int m_blk, n_blk;
         tile_coords(tile, num_m, num_n, kGroup, m_blk, n_blk);
         const int a_row = m_blk * C::kTileM + (int)rank * BM;
         const int b_row = n_blk * BN + (int)rank * C::kBRows;
-        for (int kb = 0; kb < kb_count; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, kStatusTimeoutEmpty)) { ok = false; break; }
           if constexpr (PAIR) {
             // the even CTA's full barrier expects both CTAs' bytes
@@ -695,20 +707,23 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
       int local = 0;
       bool ok = true;
       constexpr uint32_t id = idesc<KIND, BN, C::kTileM>();
-      for (int tile = unit0; ok && tile < num_tiles; tile += units, ++local) {
+      for (int w = unit0; ok && w < num_units; w += units, ++local) {
+        const int split = w - (w / splits) * splits;
+        const int kb0 = splits > 1 ? split * ea.kb_per_split : 0;
+        const int kb1 = splits > 1 ? min(kb0 + ea.kb_per_split, kb_count) : kb_count;
         const int acc = local & 1;
         const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
         if (!mbar_wait<PAIR>(&tempty[acc], acc_par ^ 1u, kStatusTimeoutAcc)) { ok = false; break; }
         fence_after();
         const uint32_t d = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < kb_count; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, kStatusTimeoutFull)) { ok = false; break; }
           fence_after();
           const uint32_t a0 = smem_u32(smA + stage * C::kABytes);
           const uint32_t b0 = smem_u32(smB + stage * C::kBBytes);
 #pragma unroll
           for (int k = 0; k < kSlab / 32; ++k)
-            mma<KIND, PAIR>(d, sdesc(a0 + 32 * k), sdesc(b0 + 32 * k), id, (kb | k) != 0 ? 1u : 0u);
+            mma<KIND, PAIR>(d, sdesc(a0 + 32 * k), sdesc(b0 + 32 * k), id, (kb != kb0 || k != 0) ? 1u : 0u);
           mma_commit<PAIR>(&empty[stage]);
           if (++stage == kStages) { stage = 0; phase ^= 1u; }
         }
@@ -740,7 +755,9 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
         else mbar_arrive(&tempty[acc]);
       }
     };
-    for (int tile = unit0; tile < num_tiles; tile += units, ++local) {
+    for (int w = unit0; w < num_units; w += units, ++local) {
+      const int tile = w / splits, split = w - tile * splits;
+      const int orow_off = split * ea.split_rows;   // this split's slice of the output
       const int acc = local & 1;
       const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
       int m_blk, n_blk;
@@ -810,7 +827,7 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
               fence_async_smem();
               __syncwarp();
               if (lane == 0) {
-                tma_store_2d(&tmO, buf, x, row0);
+                tma_store_2d(&tmO, buf, x, row0 + orow_off);
                 bulk_commit();
               }
               ++inflight;
@@ -818,7 +835,7 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
             }
           }
         } else if (row_ok) {
-          store_unit_direct(ea, row, col0, nv, r, out16);
+          store_unit_direct(ea, row + orow_off, col0, nv, r, out16);
         }
       }
       if (!released) release_acc(acc);   // this warp's columns lie past N: keep the count exact
@@ -939,7 +956,9 @@ bool make_out_map(CUtensorMap* tm, const EpiArgs& ea) {
     default: return false;
   }
   if ((reinterpret_cast<uintptr_t>(ea.out) & 15u) != 0 || ((ea.ldo * es) & 15) != 0) return false;
-  cuuint64_t dims[2] = {(cuuint64_t)ea.N, (cuuint64_t)ea.M};
+  // split-K: the stacked slices, each split_rows long
+  const int64_t rows = ea.splits > 1 ? (int64_t)ea.split_rows * ea.splits : (int64_t)ea.M;
+  cuuint64_t dims[2] = {(cuuint64_t)ea.N, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ea.ldo * es)};
   cuuint32_t box[2] = {(cuuint32_t)(128 / es), 32u};
   cuuint32_t estr[2] = {1, 1};
@@ -997,7 +1016,8 @@ int launch_t(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea,
   // gradient: coalesced read-add-store through the staging buffer
   ea.tma_out = make_out_map(&to, ea) ? 1 : 0;
   ea.coalesced_out = (!ea.tma_out && ea.accumulate && ea.vec_out) ? 1 : 0;
-  const int tiles = ((ea.M + C::kTileM - 1) / C::kTileM) * ((ea.N + BN - 1) / BN);
+  // work units: tiles x K splits
+  const int tiles = ((ea.M + C::kTileM - 1) / C::kTileM) * ((ea.N + BN - 1) / BN) * (ea.splits > 1 ? ea.splits : 1);
   if constexpr (PAIR) {
     const int cap = pair_capacity<KIND, BN, EPI, EW>();
     if (cap < 1) return APA_ERR_UNSUPPORTED;
@@ -1043,6 +1063,75 @@ int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea
               cudaStream_t s) {
   if (ew == 8) return launch_shape<KIND, EPI, 8>(A, lda, B, ldb, ea, tile, grid_cap, s);
   return launch_shape<KIND, EPI, 4>(A, lda, B, ldb, ea, tile, grid_cap, s);
+}
+
+// Split-K phase 2 for a weight gradient: sum the fp32 partial slices in
+// split order (deterministic), then exactly the weight-gradient epilogue of
+// the GEMM: counts of nonzero / underflow values (on the fp32 sum; at FP16 on
+// its fp16 rounding), the rounding to the working dtype and the fp32 store
+// (or accumulate), and the last block's ratio fold into the running max.
+template <int KIND>
+__global__ void __launch_bounds__(256) wgrad_reduce_kernel(const float* ws, int splits, int64_t slice, int64_t ld_ws,
+                                                           int rows, int cols, float* dw, int64_t lddw, int accumulate,
+                                                           float vmin, unsigned long long* counters,
+                                                           float* ratio_max) {
+  __shared__ unsigned int s_nz[8], s_uf[8];
+  const uint32_t vb = __float_as_uint(vmin);
+  unsigned int nz = 0, uf = 0;
+  const int64_t total = (int64_t)rows * cols;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+    const int64_t r = e / cols, c = e - r * cols;
+    const float* src = ws + r * ld_ws + c;
+    float acc = src[0];
+    for (int sp = 1; sp < splits; ++sp) acc += src[sp * slice];
+    float out;
+    if constexpr (KIND == KIND_E4M3) {
+      const uint32_t a = (__float_as_uint(acc) & 0x7FFFFFFFu) - 1u;
+      nz += a < 0x7F800000u ? 1u : 0u;
+      uf += a < vb - 1u ? 1u : 0u;
+      out = e4m3_to_f32(e4m3_from_f32(acc));
+    } else if constexpr (KIND == KIND_F16) {
+      out = f16_to_f32(f16_from_f32(acc));
+      const uint32_t a = (__float_as_uint(out) & 0x7FFFFFFFu) - 1u;
+      nz += a < 0x7F800000u ? 1u : 0u;
+      uf += a < vb - 1u ? 1u : 0u;
+    } else {
+      out = acc;
+    }
+    float* d = dw + r * lddw + c;
+    *d = accumulate ? *d + out : out;
+  }
+  if (!counters) return;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    nz += __shfl_xor_sync(0xFFFFFFFFu, nz, o);
+    uf += __shfl_xor_sync(0xFFFFFFFFu, uf, o);
+  }
+  if ((threadIdx.x & 31) == 0) { s_nz[threadIdx.x >> 5] = nz; s_uf[threadIdx.x >> 5] = uf; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long bnz = 0, buf = 0;
+    for (int w = 0; w < 8; ++w) { bnz += s_nz[w]; buf += s_uf[w]; }
+    if (bnz) atomicAdd(&counters[0], bnz);
+    if (buf) atomicAdd(&counters[1], buf);
+    __threadfence();
+    const unsigned long long ticket = atomicAdd(&counters[2], 1ull);
+    if (ticket == (unsigned long long)gridDim.x - 1ull) {
+      __threadfence();
+      const unsigned long long nzc = atomicAdd(&counters[0], 0ull);
+      const unsigned long long ufc = atomicAdd(&counters[1], 0ull);
+      float ratio = 0.0f;
+      if (nzc != 0ull) ratio = __fdiv_rn(__ull2float_rn(ufc), __ull2float_rn(nzc));
+      if (ratio_max) {
+        const float old = *ratio_max;
+        *ratio_max = (old != old) ? old : fmaxf(old, ratio);
+      }
+      counters[0] = 0ull;
+      counters[1] = 0ull;
+      counters[2] = 0ull;
+    }
+  }
 }
 
 template <int KIND, int EPI>
@@ -1111,6 +1200,7 @@ bool pair_possible(int rung, int epi) {
     case EPI_FWD: return pair_ok<KIND, EPI_FWD>();           \
     case EPI_DGRAD: return pair_ok<KIND, EPI_DGRAD>();       \
     case EPI_WGRAD: return pair_ok<KIND, EPI_WGRAD>();       \
+    case EPI_RAW: return pair_ok<KIND, EPI_RAW>();           \
     default: return false;                                   \
   }
   switch (rung) {
@@ -1128,7 +1218,7 @@ int resolve_plan(int rung, int epi, int64_t M, int64_t N, int64_t K, int out_dt,
                  GemmPlan* out) {
   using namespace gemm;
   if (rung != APA_RUNG_FP8 && rung != APA_RUNG_FP16 && rung != APA_RUNG_TF32) return APA_ERR_INVALID;
-  if (epi != EPI_FWD && epi != EPI_DGRAD && epi != EPI_WGRAD) return APA_ERR_INVALID;
+  if (epi != EPI_FWD && epi != EPI_DGRAD && epi != EPI_WGRAD && epi != EPI_RAW) return APA_ERR_INVALID;
   if (grid_cap <= 0 && g_gemm_sm_limit > 0) grid_cap = g_gemm_sm_limit;
   const int ew_flag = tile & 3;
   tile &= ~3;
@@ -1153,6 +1243,7 @@ int gemm_dispatch(int rung, int epi, const void* A, int64_t lda, const void* B, 
   switch (epi) {                                                                                           \
     case EPI_FWD: return launch_bn<KIND, EPI_FWD>(A, lda, B, ldb, ea, pl.tile, pl.ew, grid_cap, s);        \
     case EPI_DGRAD: return launch_bn<KIND, EPI_DGRAD>(A, lda, B, ldb, ea, pl.tile, pl.ew, grid_cap, s);    \
+    case EPI_RAW: return launch_bn<KIND, EPI_RAW>(A, lda, B, ldb, ea, pl.tile, pl.ew, grid_cap, s);        \
     default: return launch_bn<KIND, EPI_WGRAD>(A, lda, B, ldb, ea, pl.tile, pl.ew, grid_cap, s);           \
   }
   switch (rung) {
@@ -1180,6 +1271,7 @@ EpiArgs blank(int64_t M, int64_t N, int64_t K) {
   ea.out = nullptr; ea.ldo = 0; ea.out_dt = APA_DT_F32; ea.vec_out = 0; ea.tma_out = 0; ea.coalesced_out = 0;
   ea.bias = nullptr; ea.amax = nullptr; ea.flag = nullptr;
   ea.counters = nullptr; ea.ratio_max = nullptr; ea.vmin = 0.0f; ea.accumulate = 0; ea.telem = 0;
+  ea.splits = 1; ea.kb_per_split = 0; ea.split_rows = 0;
   ea.M = (int)M; ea.N = (int)N; ea.K = (int)K;
   return ea;
 }
@@ -1265,4 +1357,94 @@ extern "C" int apa_gemm_tn(int rung, int epilogue, const void* A, int64_t lda, c
   ea.out = out; ea.ldo = ldo; ea.out_dt = out_dtype;
   ea.vec_out = out_vec(out, ldo, out_dtype == APA_DT_F32 ? 4 : 2);
   return apa::gemm_dispatch(rung, epilogue, A, lda, B, ldb, ea, tile, grid_cap, static_cast<cudaStream_t>(stream));
+}
+
+namespace apa {
+
+// Split-K for a weight gradient dw[Mo, No] reduced over Kt tokens: used when
+// the tiles of the ordinary plan would keep fewer than half of the SMs busy
+// and the reduction is long; each split then covers at least 16 K slabs.
+struct SplitPlan {
+  int tile, ew, splits, kb_per_split;
+  int64_t ld_ws;       // row pitch of a slice (16-byte rows)
+  int64_t rows_pad;    // rows of a slice: the epilogue stores 32-row boxes, so a
+                       // slice is padded to a multiple of 32 and no box of one
+                       // split reaches into the next split's slice
+};
+
+SplitPlan plan_wgrad_split(int rung, int64_t Mo, int64_t No, int64_t Kt) {
+  using namespace gemm;
+  SplitPlan sp{0, 0, 1, 0, 0, 0};
+  const int es = rung == APA_RUNG_FP8 ? 1 : rung == APA_RUNG_FP16 ? 2 : 4;
+  const int slots = g_gemm_sm_limit > 0 ? g_gemm_sm_limit : num_sms();
+  GemmPlan pl = plan_gemm(Mo, No, Kt, es, 4, slots, false, 0);
+  auto cdiv = [](int64_t a, int64_t b) { return (a + b - 1) / b; };
+  const int64_t tiles = cdiv(Mo, 128) * cdiv(No, pl.tile == kTile128 ? 128 : 256);
+  const int64_t kb_count = cdiv(Kt * es, kSlab);
+  if (tiles * 2 > slots) return sp;
+  int64_t S = std::min<int64_t>(std::min<int64_t>(slots / tiles, 8), kb_count / 16);
+  if (S < 2) return sp;
+  const int64_t per = cdiv(kb_count, S);
+  S = cdiv(kb_count, per);
+  if (S < 2) return sp;
+  sp.tile = pl.tile;
+  sp.ew = 8;   // a single wave: the epilogue is exposed
+  sp.splits = (int)S;
+  sp.kb_per_split = (int)per;
+  sp.ld_ws = (No + 3) / 4 * 4;
+  sp.rows_pad = (Mo + 31) / 32 * 32;
+  return sp;
+}
+
+}  // namespace apa
+
+extern "C" int apa_wgrad_workspace_bytes(int rung, int64_t M, int64_t N, int64_t K, int64_t* bytes_out) {
+  if (!bytes_out) return APA_ERR_INVALID;
+  if (int st = check_dims(N, K, M)) return st;
+  if (rung != APA_RUNG_FP8 && rung != APA_RUNG_FP16 && rung != APA_RUNG_TF32) return APA_ERR_INVALID;
+  const apa::SplitPlan sp = apa::plan_wgrad_split(rung, N, K, M);
+  *bytes_out = sp.splits > 1 ? (int64_t)sp.splits * sp.rows_pad * sp.ld_ws * 4 : 0;
+  return APA_OK;
+}
+
+extern "C" int apa_linear_wgrad_ws(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt, float* dw,
+                                   int64_t lddw, int64_t M, int64_t N, int64_t K, int accumulate,
+                                   unsigned long long* counters, float* ratio_max, void* workspace,
+                                   int64_t workspace_bytes, void* stream) {
+  if (int st = check_dims(N, K, M)) return st;
+  if (!dyqt || !xqt || !dw || lddw < K || lddyt < M || ldxt < M) return APA_ERR_INVALID;
+  if (rung != APA_RUNG_TF32 && !counters) return APA_ERR_INVALID;
+  const apa::SplitPlan sp = apa::plan_wgrad_split(rung, N, K, M);
+  const int64_t need = sp.splits > 1 ? (int64_t)sp.splits * sp.rows_pad * sp.ld_ws * 4 : 0;
+  if (need == 0 || !workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15u))
+    return apa_linear_wgrad(rung, dyqt, lddyt, xqt, ldxt, dw, lddw, M, N, K, accumulate, counters, ratio_max,
+                            stream);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // phase 1: raw fp32 partial sums, one slice per split
+  EpiArgs ea = blank(N, K, M);
+  ea.out = workspace; ea.ldo = sp.ld_ws; ea.out_dt = APA_DT_F32; ea.vec_out = 1;
+  ea.splits = sp.splits; ea.kb_per_split = sp.kb_per_split; ea.split_rows = (int)sp.rows_pad;
+  const int tile = sp.tile | (sp.ew == 8 ? apa::gemm::kEpiFlag8 : apa::gemm::kEpiFlag4);
+  if (int st = apa::gemm_dispatch(rung, apa::gemm::EPI_RAW, dyqt, lddyt, xqt, ldxt, ea, tile, 0, s)) return st;
+  // phase 2: ordered sum + the weight-gradient epilogue
+  const float vmin = rung == APA_RUNG_FP8 ? 0.015625f : rung == APA_RUNG_FP16 ? 6.1035e-5f : 0.0f;
+  const int64_t total = N * K;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)apa::num_sms() * 4));
+  const float* ws = static_cast<const float*>(workspace);
+  const int64_t slice = sp.rows_pad * sp.ld_ws;
+  using namespace apa::gemm;
+  switch (rung) {
+    case APA_RUNG_FP8:
+      wgrad_reduce_kernel<KIND_E4M3><<<grid, 256, 0, s>>>(ws, sp.splits, slice, sp.ld_ws, (int)N, (int)K, dw, lddw,
+                                                          accumulate, vmin, counters, ratio_max);
+      break;
+    case APA_RUNG_FP16:
+      wgrad_reduce_kernel<KIND_F16><<<grid, 256, 0, s>>>(ws, sp.splits, slice, sp.ld_ws, (int)N, (int)K, dw, lddw,
+                                                         accumulate, vmin, counters, ratio_max);
+      break;
+    default:
+      wgrad_reduce_kernel<KIND_TF32><<<grid, 256, 0, s>>>(ws, sp.splits, slice, sp.ld_ws, (int)N, (int)K, dw, lddw,
+                                                          accumulate, vmin, counters, ratio_max);
+  }
+  return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }

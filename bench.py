@@ -55,6 +55,49 @@ def peaks():
     return p
 
 
+def library_peaks(torch, dev):
+    """Dense GEMM throughput of the vendor libraries on this GPU, a second
+    reference for the rung rooflines: cuBLASLt FP8 (torch._scaled_mm, E4M3 x
+    E4M3, unit scales, bf16 out), cuBLAS fp16 and TF32 (fp32 inputs with TF32
+    math) at 8192^3, best of a few back-to-back launches (burst, like the bf16
+    figure of MEASURED_PEAKS.json)."""
+    n = 8192
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(7)
+    a32 = torch.randn(n, n, device=dev, generator=g)
+    b32 = torch.randn(n, n, device=dev, generator=g)
+
+    def best(fn, reps=10):
+        for _ in range(3):
+            fn()
+        t = []
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            t.append(e0.elapsed_time(e1))
+        return 2.0 * n ** 3 / (min(t) * 1e-3) / 1e12
+
+    try:
+        a8, b8 = a32.to(torch.float8_e4m3fn), b32.to(torch.float8_e4m3fn).t()
+        one = torch.ones((), device=dev)
+        out["fp8_tflops"] = round(best(lambda: torch._scaled_mm(a8, b8, scale_a=one, scale_b=one,
+                                                                out_dtype=torch.bfloat16)), 1)
+    except Exception as e:   # the library path is only a reference denominator
+        out["fp8_error"] = repr(e)[:120]
+    a16, b16 = a32.half(), b32.half()
+    out["fp16_tflops"] = round(best(lambda: a16 @ b16), 1)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    out["tf32_tflops"] = round(best(lambda: a32 @ b32), 1)
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del a32, b32
+    torch.cuda.empty_cache()
+    return out
+
+
 class ClockSampler:
     """nvidia-smi samples during the timed region (SM clock and throttle reasons)."""
 
@@ -157,6 +200,7 @@ def run_ours(args):
     launches = 0
     clocks = None
     pk = peaks()
+    libpk = library_peaks(torch, dev) if rank == 0 else {}
     gstep = None
     from apa.graphs import GraphedTrainStep
     for level, name in ((0, "fp8"), (1, "fp16"), (2, "tf32")):
@@ -206,8 +250,10 @@ def run_ours(args):
             launches = (_lib.calls - c0) + (0 if args.eager else args.steps * gstep.captured_launches)
         results[name] = {"ms_per_step": ms, "tflops": world * FLOPS_STEP / ms / 1e9,
                          "frac_of_peak": FLOPS_STEP / ms / 1e9 / pk[f"{name}_tflops"]}
+        if f"{name}_tflops" in libpk:
+            results[name]["frac_of_library_gemm"] = FLOPS_STEP / ms / 1e9 / libpk[f"{name}_tflops"]
         if level == 0:
-            gemm_roof = time_gemm(torch, _lib, lin, xr, dev, pk)
+            gemm_roof = time_gemm(torch, _lib, lin, xr, dev, pk, libpk)
         # graphs holding NCCL work must be released before the process group
         gstep = step = None
         del lin, mgr
@@ -232,7 +278,10 @@ def run_ours(args):
                                                 launch="eager" if args.eager else
                                                 "cuda-graph replay of pre_step+fwd+bwd, ladder eager"),
             "rungs": {k: {"tflops": round(v["tflops"], 2), "ms_per_step": round(v["ms_per_step"], 4),
-                          "frac_of_peak": round(v["frac_of_peak"], 4)} for k, v in results.items()},
+                          "frac_of_peak": round(v["frac_of_peak"], 4),
+                          "frac_of_library_gemm": round(v.get("frac_of_library_gemm", 0.0), 4)}
+                      for k, v in results.items()},
+            "library_gemm_peaks": libpk,
             "roofline": gemm_roof,
             "e2e": e2e,
             "gpt": gpt,
@@ -426,7 +475,7 @@ def run_gpt(torch, dist, name, world, rank, dev, steps, warmup, barrier, max_ove
     return out
 
 
-def time_gemm(torch, _lib, lin, xr, dev, pk):
+def time_gemm(torch, _lib, lin, xr, dev, pk, libpk):
     """The dominant kernel: the FP8 tcgen05 GEMM (forward, 8192x4096x4096),
     timed alone with CUDA events on its launching stream. Also times the same
     GEMM without bias twice, with the fused telemetry (amax / NaN flag of y)
@@ -469,6 +518,7 @@ def time_gemm(torch, _lib, lin, xr, dev, pk):
         t_bare.append(timed(bare, 30))
     tel, bar = min(t_tel), min(t_bare)
     achieved = 2.0 * M * N * K / (us * 1e-6) / 1e12
+    lib_fp8 = libpk.get("fp8_tflops")
     tile, ew = ctypes.c_int(0), ctypes.c_int(0)
     _lib.check(lib.apa_gemm_plan(0, 0, M, N, K, _lib.DT_F32, 0, 0, ctypes.addressof(tile), ctypes.addressof(ew)),
                "plan")
@@ -477,6 +527,7 @@ def time_gemm(torch, _lib, lin, xr, dev, pk):
             "bound": "tensor",
             "achieved": round(achieved, 1), "peak": pk["fp8_tflops"], "unit": "TFLOP/s",
             "frac": round(achieved / pk["fp8_tflops"], 4), "us_per_launch": round(us, 2),
+            "frac_of_library_fp8": round(achieved / lib_fp8, 4) if lib_fp8 else None,
             "peak_note": f"2 x {pk['source']} bf16 cuBLAS burst ({pk['bf16_tflops']} TFLOP/s); "
                          "spec dense FP8 4500 TFLOP/s",
             "telemetry": {"us_with": round(tel, 2), "us_bare": round(bar, 2),

@@ -43,6 +43,7 @@ extern "C" {
 #define APA_EPI_FWD 0
 #define APA_EPI_DGRAD 1
 #define APA_EPI_WGRAD 2
+#define APA_EPI_RAW 3   /* plain fp32 accumulator (split-K partials, bare timing) */
 
 /* Library ABI version (bumped on any signature change). */
 int apa_abi_version(void);
@@ -155,6 +156,27 @@ int apa_linear_dgrad(int rung, const void* dyq, int64_t lddy, const void* wqt, i
 int apa_linear_wgrad(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt,
                      float* dw, int64_t lddw, int64_t M, int64_t N, int64_t K, int accumulate,
                      unsigned long long* counters, float* ratio_max, void* stream);
+
+/*
+ * Scratch bytes apa_linear_wgrad_ws uses for this shape (same M, N, K as
+ * apa_linear_wgrad), 0 when the weight gradient is not split.
+ */
+int apa_wgrad_workspace_bytes(int rung, int64_t M, int64_t N, int64_t K, int64_t* bytes_out);
+
+/*
+ * apa_linear_wgrad with a caller-owned scratch buffer (16-byte aligned,
+ * apa_wgrad_workspace_bytes long): when the weight gradient's tiles would
+ * leave most SMs idle (small N x K, many tokens), the reduction over tokens is
+ * split into up to 8 parts computed in parallel as fp32 partial sums, then
+ * summed in split order by a second kernel that applies the same epilogue
+ * (underflow counts, rounding to the working dtype, overwrite or accumulate,
+ * ratio fold). Without enough scratch it behaves exactly like
+ * apa_linear_wgrad. Same reference interfaces as apa_linear_wgrad.
+ */
+int apa_linear_wgrad_ws(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt,
+                        float* dw, int64_t lddw, int64_t M, int64_t N, int64_t K, int accumulate,
+                        unsigned long long* counters, float* ratio_max, void* workspace,
+                        int64_t workspace_bytes, void* stream);
 
 /*
  * Cap the number of CTAs (SMs) the persistent GEMMs use; 0 restores one CTA
