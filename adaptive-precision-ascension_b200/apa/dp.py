@@ -39,12 +39,39 @@ class _Bucket:
 RESERVED_SMS = 16
 
 
+def _capped_nccl_group(process_group, max_ctas: int):
+    """A second NCCL communicator over the same ranks whose kernels use at most
+    max_ctas CTAs: a long backward can then carry the reductions on a few SMs
+    instead of losing a large share of every SM-wide kernel to them."""
+    ranks = dist.get_process_group_ranks(process_group) if process_group is not None else list(
+        range(dist.get_world_size()))
+    opts = dist.ProcessGroupNCCL.Options()
+    opts.config.max_ctas = max_ctas
+    opts.config.min_ctas = 1
+    opts.config.nvls_ctas = max_ctas
+    return dist.new_group(ranks=ranks, backend="nccl", pg_options=opts, use_local_synchronization=True)
+
+
 class GradientAverager:
-    def __init__(self, mgr, process_group=None, bucket_bytes: int = 64 << 20):
-        self.pg = process_group
+    def __init__(self, mgr, process_group=None, bucket_bytes: int = 64 << 20, reserved_sms: int = RESERVED_SMS,
+                 max_ctas: int = 0):
         self.world = dist.get_world_size(process_group)
+        if max_ctas > 0 and dist.get_backend(process_group) == "nccl":
+            process_group = _capped_nccl_group(process_group, max_ctas)
+            reserved_sms = max_ctas
+        self.pg = process_group
+        self.reserved_sms = reserved_sms
         self.avg_op = dist.ReduceOp.AVG if dist.get_backend(process_group) == "nccl" else None
-        params = [p for p in mgr.get_trainable_parameters() if p.dtype == torch.float32]
+        # buckets follow the order in which backward produces gradients, which
+        # is close to the reverse of registration (module definition) order;
+        # buckets are issued strictly in order, so one bucket holding an early
+        # layer's gradient would hold back every bucket after it
+        trainable = {id(p) for p in mgr.get_trainable_parameters() if p.dtype == torch.float32}
+        params, seen = [], set()
+        for p in mgr.model.parameters():
+            if id(p) in trainable and id(p) not in seen:
+                params.append(p)
+                seen.add(id(p))
         params = list(reversed(params))
         device = params[0].device if params else torch.device("cpu")
         self.buckets: List[_Bucket] = []
@@ -67,6 +94,8 @@ class GradientAverager:
         self.graphed = False
         self.comm_stream = None        # forked stream for reductions captured in a CUDA graph
         self.capture_fork = False
+        self.ready_count = 0           # gradients marked ready in this step
+        self.launch_marks: List[int] = []   # ready_count at each bucket launch (overlap check)
         apa_params = set()
         for m in mgr.apa_modules.values():
             m._grad_ready_cb = self._apa_ready
@@ -90,6 +119,8 @@ class GradientAverager:
             b.pending = len(b.params)
             b.handle = None
         self.next = 0
+        self.ready_count = 0
+        self.launch_marks = []
         self.armed = True
 
     def _mark(self, p):
@@ -98,6 +129,7 @@ class GradientAverager:
             return
         b = self.buckets[bi]
         b.pending -= 1
+        self.ready_count += 1
         self._launch_ready()
 
     def _apa_ready(self, mod):
@@ -112,12 +144,13 @@ class GradientAverager:
         if self.buckets and self.buckets[0].flat.is_cuda:
             from . import _lib
             n = 0
-            if on:
+            if on and self.reserved_sms > 0:
                 n = max(1, torch.cuda.get_device_properties(self.buckets[0].flat.device).multi_processor_count
-                        - RESERVED_SMS)
+                        - self.reserved_sms)
             _lib.check(_lib.lib().apa_set_gemm_sm_limit(n), "apa_set_gemm_sm_limit")
 
     def _launch(self, b: _Bucket):
+        self.launch_marks.append(self.ready_count)
         if not self.limited:
             self._limit_gemms(True)
             self.limited = True

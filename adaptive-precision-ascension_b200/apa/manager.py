@@ -87,7 +87,8 @@ class _LadderState:
 
 class APAManager:
     def __init__(self, model: nn.Module, config: APAConfig = APAConfig(), process_group=None,
-                 sync_gradients: bool = True, bucket_bytes: int = 64 << 20):
+                 sync_gradients: bool = True, bucket_bytes: int = 64 << 20, dp_reserved_sms: int = 16,
+                 dp_max_ctas: int = 0):
         self.model = model
         self.config = config
         self.step_count = 0
@@ -107,6 +108,8 @@ class APAManager:
         self._telem_pg = None          # second communicator for the small telemetry reduction
         self._sync_gradients = sync_gradients
         self._bucket_bytes = bucket_bytes
+        self._dp_reserved_sms = dp_reserved_sms   # SMs the GEMMs leave free while a reduction runs
+        self._dp_max_ctas = dp_max_ctas           # >0: gradient communicator capped at this many CTAs
         self._dp = None
 
     # ------------------------------------------------------------------
@@ -409,7 +412,8 @@ class APAManager:
     def _averager(self):
         from .dp import GradientAverager
         if self._dp is None:
-            self._dp = GradientAverager(self, self._pg, self._bucket_bytes)
+            self._dp = GradientAverager(self, self._pg, self._bucket_bytes, self._dp_reserved_sms,
+                                        self._dp_max_ctas)
         return self._dp
 
     def _allreduce_grads(self):

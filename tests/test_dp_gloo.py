@@ -93,6 +93,62 @@ def test_gradient_averager_two_ranks():
             assert torch.allclose(a0, want, atol=1e-6) and torch.equal(a0, a1)
 
 
+class _ApaFirstManager(_FakeManager):
+    """Lists parameters the way APAManager.get_trainable_parameters does:
+    the layers it manages first, every other parameter after."""
+
+    def get_trainable_parameters(self):
+        ps = list(self.model.parameters())
+        return ps[2:] + ps[:2]
+
+
+def _order_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from apa.dp import GradientAverager
+        torch.manual_seed(0)
+        # an embedding registered first: its gradient is produced last by backward
+        model = nn.Sequential(nn.Embedding(50, 16), nn.Linear(16, 16), nn.ReLU(), nn.Linear(16, 8))
+        avg = GradientAverager(_ApaFirstManager(model), None, bucket_bytes=256)
+        avg.arm()
+        idx = torch.randint(0, 50, (12,), generator=torch.Generator().manual_seed(rank))
+        model(idx).pow(2).sum().backward()
+        marks, total = list(avg.launch_marks), avg.ready_count
+        sizes = [len(b.params) for b in avg.buckets]
+        avg.finish()
+        q.put((rank, marks, total, sizes))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_buckets_follow_backward_order_two_ranks():
+    """Buckets are issued strictly in order; the first one must go out before
+    the last gradient exists (buckets built from the manager's listing would
+    put the embedding first and hold every reduction to the end of backward)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_order_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict((r[0], r[1:]) for r in (q.get(timeout=120) for _ in procs))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in (0, 1):
+        marks, total, sizes = out[r]
+        assert len(sizes) > 2 and len(marks) == len(sizes)
+        # each bucket goes out as soon as its own gradients exist (weight and
+        # bias of one layer may arrive in either order)
+        cum = 0
+        for m, n in zip(marks, sizes):
+            cum += n
+            assert m <= cum + 1, (marks, sizes)
+        assert marks[0] < total
+
+
 def _telemetry_worker(rank, world, port, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
