@@ -29,6 +29,7 @@ grad copy to the masters are all folded into those launches.
 from __future__ import annotations
 
 import ctypes
+import weakref
 
 import math
 from typing import Optional
@@ -139,6 +140,27 @@ class _BoundaryCastFn(torch.autograd.Function):
     def backward(ctx, g):
         # ToCopyBackward: the gradient returns in the source dtype
         return g.to(ctx.src_dtype), None
+
+
+# dgrad outputs of this step whose amax / NaN telemetry the dgrad kernel has
+# already folded into the layer's boundary-cast buffers: data_ptr -> (weak
+# reference to the dx tensor, boundary-cast module). A leaf module whose
+# grad_output is one of these tensors (a LayerNorm or GELU feeding exactly one
+# APALinear) merges that telemetry instead of reading the tensor again
+# (manager.py:70-84 hooks). Cleared by APAManager.pre_step.
+_DGRAD_TELEMETRY: dict = {}
+
+
+def dgrad_telemetry_source(g):
+    """The boundary-cast module whose buffers hold the telemetry of tensor g,
+    when g is a live dgrad output of this step; else None."""
+    e = _DGRAD_TELEMETRY.get(g.data_ptr())
+    if e is None:
+        return None
+    t = e[0]()
+    if t is None or t.data_ptr() != g.data_ptr() or t.shape != g.shape or t.dtype != g.dtype:
+        return None
+    return e[1]
 
 
 class _APALinearFn(torch.autograd.Function):
@@ -310,6 +332,10 @@ class _APALinearFn(torch.autograd.Function):
                                       _lib.ptr(getattr(bc, "gpu_has_nonfinite", None)), s)
             _lib.check(st, "apa_linear_dgrad")
             dx = dx.view(*ctx.lead, K)
+            # the kernel's telemetry is taken on the working-dtype values; dx
+            # holds them exactly when it is fp32 or the working dtype itself
+            if ctx.xdtype == torch.float32 or ctx.xdtype == mod.working_dtype:
+                _DGRAD_TELEMETRY[dx.data_ptr()] = (weakref.ref(dx), bc)
         if f_on and dx is not None:
             _update_forensic_role(dx, "grad_input", *mod._forensic_args())
         mod._needs_wt = need_dx

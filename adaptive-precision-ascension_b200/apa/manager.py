@@ -37,6 +37,7 @@ import torch.nn as nn
 from . import _lib
 from .config import APAConfig, LEVEL_FP8, LEVEL_FP16, LEVEL_TF32, THRESHOLDS_MAX
 from .layers import APALinear
+from .layers import dgrad_telemetry_source, _DGRAD_TELEMETRY
 from .telemetry import APAEventLogger, APAForensicLogger, track_telemetry_on_tensor
 
 _LEVEL_NAME = {LEVEL_FP8: "FP8", LEVEL_FP16: "FP16", LEVEL_TF32: "TF32"}
@@ -128,7 +129,19 @@ class APAManager:
 
                 def hook_fn(mod, grad_input, grad_output):
                     for g in grad_output:
-                        if g is not None:
+                        if g is None:
+                            continue
+                        src = dgrad_telemetry_source(g) if g.is_cuda else None
+                        if src is not None:
+                            # g is an APALinear's dgrad output whose telemetry is
+                            # already in its boundary-cast buffers: both modules'
+                            # buffers see the same values and are reset together
+                            _lib.check(_lib.lib().apa_merge_telemetry(mod.gpu_amax.data_ptr(),
+                                                                      mod.gpu_has_nonfinite.data_ptr(),
+                                                                      src.gpu_amax.data_ptr(),
+                                                                      _lib.stream_handle(g.device)),
+                                       "apa_merge_telemetry")
+                        else:
                             track_telemetry_on_tensor(g, mod.gpu_amax, mod.gpu_has_nonfinite)
 
                 # APALinear fuses its boundary cast into its kernels (the cast
@@ -186,6 +199,7 @@ class APAManager:
     def pre_step(self):
         """Zero the per-step flags (not amax: it persists across the check
         window) and refresh every working copy (manager.py:145-172)."""
+        _DGRAD_TELEMETRY.clear()
         st = self._state()
         s = _lib.stream_handle(self._global_nonfinite.device)
         _lib.check(_lib.lib().apa_zero_list(st.zero.data_ptr(), st.nzero, s), "apa_zero_list")
