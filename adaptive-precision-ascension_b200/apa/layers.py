@@ -29,11 +29,11 @@ grad copy to the masters are all folded into those launches.
 from __future__ import annotations
 
 import ctypes
-import weakref
-
 import math
+import weakref
 from typing import Optional
 
+import numpy as np
 import torch
 import torch.nn as nn
 
@@ -85,23 +85,31 @@ def _alloc_2d(rows: int, cols: int, dtype: torch.dtype, device) -> torch.Tensor:
     return torch.empty(rows, ld, dtype=dtype, device=device)[:, :cols]
 
 
-def _update_forensic_role(tensor, role, f_amax, f_shape, f_stats, capture_argmax, f_argmax):
-    """Per-role statistics for forensic mode (apa/layers.py:63-106). Opt-in and
-    slow by design: every statistic is read back to the host."""
-    if f_amax is None:
+_STATS_DTYPES = (torch.float32, torch.float16, torch.bfloat16, torch.float8_e4m3fn)
+
+
+def _update_forensic_role(tensor, role, mod):
+    """Per-role statistics for forensic mode (apa/layers.py:63-106): max |x|,
+    its first flat index, mean and standard deviation, computed on the device
+    into the module's record for the role with no host synchronisation; the
+    host reads the records only when a forensic snapshot needs them
+    (APALinear._forensic_sync)."""
+    if not mod.config.enable_forensic_logging:
         return
     with torch.no_grad():
         t = tensor.detach()
-        if t.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+        if t.dtype not in _STATS_DTYPES:
             t = t.to(torch.float32)
-        a = t.abs()
-        f_amax[role] = a.max().item()
-        f_shape[role] = list(tensor.shape)
-        if f_stats is not None:
-            tf = t.float()
-            f_stats[role] = {"mean": tf.mean().item(), "std": tf.std().item() if tf.numel() > 1 else 0.0}
-        if capture_argmax and f_argmax is not None:
-            f_argmax[role] = int(a.flatten().argmax().item())
+        if not t.is_contiguous():
+            t = t.contiguous()
+        rec = mod._forensic_dev.get(role)
+        if rec is None or rec.device != t.device:
+            rec = torch.zeros(5, dtype=torch.int64, device=t.device)
+            mod._forensic_dev[role] = rec
+        _lib.check(_lib.lib().apa_tensor_stats(t.data_ptr(), _lib.dt_code(t.dtype), t.numel(), rec.data_ptr(),
+                                               _lib.stream_handle(t.device)), "apa_tensor_stats")
+        mod._forensic_last_shape[role] = list(tensor.shape)
+        mod._forensic_pending.add(role)
 
 
 class APABoundaryCast(nn.Module):
@@ -219,10 +227,9 @@ class _APALinearFn(torch.autograd.Function):
         _lib.check(st, "apa_linear_fwd")
 
         if f_on:
-            f = mod._forensic_args()
-            _update_forensic_role(xq, "input_activation", *f)
-            _update_forensic_role(mod.weight_work, "weight", *f)
-            _update_forensic_role(y, "output", *f)
+            _update_forensic_role(xq, "input_activation", mod)
+            _update_forensic_role(mod.weight_work, "weight", mod)
+            _update_forensic_role(y, "output", mod)
 
         ctx.mod = mod
         ctx.level = level
@@ -268,7 +275,7 @@ class _APALinearFn(torch.autograd.Function):
 
         f_on = mod.config.enable_forensic_logging
         if f_on:
-            _update_forensic_role(grad_output, "grad_output", *mod._forensic_args())
+            _update_forensic_role(grad_output, "grad_output", mod)
 
         first = mod._grad_epoch != mod._epoch
         mod._grad_epoch = mod._epoch
@@ -302,7 +309,7 @@ class _APALinearFn(torch.autograd.Function):
             if W.grad is None:
                 W.grad = g
             if f_on:
-                _update_forensic_role(g, "grad_weight", *mod._forensic_args())
+                _update_forensic_role(g, "grad_weight", mod)
         if need_db:
             b = mod.bias_master
             g = b.grad
@@ -337,7 +344,7 @@ class _APALinearFn(torch.autograd.Function):
             if ctx.xdtype == torch.float32 or ctx.xdtype == mod.working_dtype:
                 _DGRAD_TELEMETRY[dx.data_ptr()] = (weakref.ref(dx), bc)
         if f_on and dx is not None:
-            _update_forensic_role(dx, "grad_input", *mod._forensic_args())
+            _update_forensic_role(dx, "grad_input", mod)
         mod._needs_wt = need_dx
         ctx.xqt = None
         ctx.wqt = None
@@ -383,6 +390,8 @@ class APALinear(nn.Module):
         self._forensic_last_shape: dict = {}
         self._forensic_role_stats: dict = {}
         self._forensic_role_argmax: dict = {}
+        self._forensic_dev: dict = {}          # role -> 5-word device record (apa_tensor_stats)
+        self._forensic_pending: set = set()    # roles with device records newer than the dicts
         # working-copy buffers (recreated when the level changes)
         self._wq = None
         self._wqt = None
@@ -495,19 +504,37 @@ class APALinear(nn.Module):
     # ------------------------------------------------------------------
     # telemetry entry points kept from the reference
     # ------------------------------------------------------------------
-    def _forensic_args(self):
+    def _forensic_sync(self):
+        """Read the device records of the roles updated since the last read
+        (one copy) into the per-role dictionaries the forensic snapshot uses:
+        amax, and when configured mean/std (unbiased) and the argmax index."""
+        if not self._forensic_pending:
+            return
         c = self.config
-        return (self._forensic_role_amax, self._forensic_last_shape,
-                self._forensic_role_stats if c.forensic_capture_tensor_stats else None,
-                c.forensic_capture_argmax_index,
-                self._forensic_role_argmax if c.forensic_capture_argmax_index else None)
+        roles = sorted(self._forensic_pending)
+        words = torch.stack([self._forensic_dev[r] for r in roles]).cpu().numpy().view(np.uint64)
+        for role, w in zip(roles, words):
+            key = int(w[0])
+            amax = float(np.array([key >> 32], dtype=np.uint32).view(np.float32)[0])
+            s1 = float(w[1:2].view(np.float64)[0])
+            s2 = float(w[2:3].view(np.float64)[0])
+            n = int(w[3])
+            self._forensic_role_amax[role] = amax
+            if c.forensic_capture_tensor_stats:
+                mean = s1 / n if n else float("nan")
+                std = math.sqrt(max((s2 - s1 * s1 / n) / (n - 1), 0.0)) if n > 1 and math.isfinite(s1) else (
+                    float("nan") if n > 1 else 0.0)
+                self._forensic_role_stats[role] = {"mean": mean, "std": std}
+            if c.forensic_capture_argmax_index:
+                self._forensic_role_argmax[role] = (~key) & 0xFFFFFFFF
+        self._forensic_pending.clear()
 
     def track_telemetry(self, tensor: torch.Tensor, role: str = "unspecified"):
         """Running max of |tensor| into gpu_amax and the NaN/Inf flag
         (apa/layers.py:374-402); ``role`` matters only in forensic mode."""
         track_telemetry_on_tensor(tensor, self.gpu_amax, self.gpu_has_nonfinite)
         if self.config.enable_forensic_logging:
-            _update_forensic_role(tensor, role, *self._forensic_args())
+            _update_forensic_role(tensor, role, self)
 
     def update_underflow_metric(self, grad: torch.Tensor):
         """gpu_underflow_ratio = max(gpu_underflow_ratio, underflow ratio of grad)

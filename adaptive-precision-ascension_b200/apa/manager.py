@@ -211,6 +211,7 @@ class APAManager:
             self._forward_execution_order.clear()
             for module in self.apa_modules.values():
                 module._forensic_role_amax.clear()
+                module._forensic_pending.clear()
 
     def _sync_grads_to_master(self):
         """The weight-gradient kernels write the fp32 master gradients directly
@@ -339,6 +340,7 @@ class APAManager:
             self._capture_forensic_snapshot(name, module, reason, old_level, trigger_value)
 
     def _capture_forensic_snapshot(self, name, module, reason, old_level, trigger_value):
+        module._forensic_sync()
         role_amax = dict(module._forensic_role_amax)
         culprit_role, culprit_amax = None, -1.0
         for role, val in role_amax.items():

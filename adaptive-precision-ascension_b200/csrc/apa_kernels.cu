@@ -6,3 +6,4 @@
 #include "cast_tma.cu"
 #include "ladder.cu"
 #include "noalloc.cu"
+#include "forensic.cu"

@@ -217,6 +217,16 @@ int apa_gemm_plan(int rung, int epilogue, int64_t M, int64_t N, int64_t K, int o
                   int grid_cap, int* tile_out, int* epi_warps_out);
 
 /*
+ * Forensic statistics of a flat tensor of n elements (n < 2^32) into a
+ * 5-word device record (zeroed here): [0] (max |x| fp32 bits << 32) | ~index
+ * of its first occurrence (NaN ranks largest), [1] sum and [2] sum of squares
+ * as fp64, [3] n, [4] 1 if any element is NaN or infinite. No host
+ * synchronisation. Replaces the per-tensor .item() reads of forensic mode
+ * (layers.py:63-106: amax, mean, std, argmax per tensor role).
+ */
+int apa_tensor_stats(const void* src, int dtype, int64_t n, unsigned long long* record, void* stream);
+
+/*
  * Bias gradient without any device allocation: db[c] = f32(cast(sum_r
  * f32(cast(dy[r, c], work)), work)) (or += when accumulate != 0), the same
  * result as apa_cast with colsum_partial followed by apa_colsum_finalize.
