@@ -23,6 +23,7 @@ EPI_FWD, EPI_DGRAD, EPI_WGRAD, EPI_RAW = 0, 1, 2, 3
 _VP = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I = ctypes.c_int
+_F = ctypes.c_float
 
 # name -> argtypes (all entry points return int status unless noted)
 SIGNATURES = {
@@ -44,6 +45,8 @@ SIGNATURES = {
     "apa_gemm_tn": [_I, _I, _VP, _I64, _VP, _I64, _VP, _I, _I64, _I64, _I64, _I64, _I, _I, _VP],
     "apa_gemm_plan": [_I, _I, _I64, _I64, _I64, _I, _I, _I, _VP, _VP],
     "apa_tensor_stats": [_VP, _I, _I64, _VP, _VP],
+    "apa_adamw_cast": [_VP, _VP, _VP, _VP, _I64, _I64, _I64, _F, _F, _F, _F, _F, _I64, _VP, _I, _I64, _VP, _I64,
+                       _VP, _VP],
     "apa_bias_grad_noalloc": [_VP, _I, _I64, _I64, _I64, _I, _VP, _I, _VP],
     "apa_ladder_pack": [_I, _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP],
     "apa_ladder_eval": [_I, _VP, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _I64, _I64,

@@ -384,6 +384,10 @@ class APALinear(nn.Module):
         # pre_step and merged at the next forward; the wgrad underflow counters
         self.register_buffer("_w_pending", torch.zeros(1, dtype=torch.float32, device=dev), persistent=False)
         self.register_buffer("_uf_counters", torch.zeros(3, dtype=torch.int64, device=dev), persistent=False)
+        # weight amax of a working copy written by the fused optimizer step
+        self.register_buffer("_w_pending_opt", torch.zeros(1, dtype=torch.float32, device=dev), persistent=False)
+        self._prerefreshed = False     # the optimizer wrote the next working copy (APAAdamW)
+        self._prerefresh_key = None
         self.ema_underflow_ratio = 0.0
         self.boundary_cast = APABoundaryCast(self)
         self._forensic_role_amax: dict = {}
@@ -463,12 +467,20 @@ class APALinear(nn.Module):
             if self._wq_level != level or self._wqt is None or self._wqt.dtype != wd:
                 self._wqt = _alloc_2d(K, N, wd, W.device)
             want_t = self._needs_wt
-            st = lib.apa_cast(W.data_ptr(), _lib.DT_F32, N, K, W.stride(0),
-                              self._wq.data_ptr() if new_wq else None, _operand_code(level), self._wq.stride(0),
-                              self._wqt.data_ptr() if want_t else None, self._wqt.stride(0),
-                              self._w_pending.data_ptr(), None, 0, None, None, s)
-            _lib.check(st, "apa_cast(weight)")
-            self._wqt_stale = not want_t
+            if self._prerefreshed and self._prerefresh_key == (level, W._version, W.data_ptr()):
+                # the fused optimizer step already wrote this working copy (and
+                # its transpose if the backward wanted one) and its amax
+                _lib.check(lib.apa_merge_telemetry(self._w_pending.data_ptr(), None,
+                                                   self._w_pending_opt.data_ptr(), s), "apa_merge_telemetry")
+                self._wqt_stale = not self._prerefresh_t
+            else:
+                st = lib.apa_cast(W.data_ptr(), _lib.DT_F32, N, K, W.stride(0),
+                                  self._wq.data_ptr() if new_wq else None, _operand_code(level), self._wq.stride(0),
+                                  self._wqt.data_ptr() if want_t else None, self._wqt.stride(0),
+                                  self._w_pending.data_ptr(), None, 0, None, None, s)
+                _lib.check(st, "apa_cast(weight)")
+                self._wqt_stale = not want_t
+            self._prerefreshed = False
             if self.bias_master is not None:
                 b = self.bias_master
                 if level == LEVEL_TF32:
@@ -482,6 +494,38 @@ class APALinear(nn.Module):
                     _lib.check(st, "apa_cast(bias)")
                     self.bias_work = self._bq
         self._wq_level = level
+
+    def _adamw_refresh(self, p, g, m, v, lr, beta1, beta2, eps, weight_decay, step) -> bool:
+        """One AdamW step of weight_master fused with the next step's working
+        copy (apa_adamw_cast): p, m, v updated in place, W_q (and W_q^T when
+        the backward uses it) written at the current level, the weight amax
+        kept for the next pre_step. False when the kernel cannot take this
+        layout; the caller then updates p itself and pre_step casts as usual."""
+        W = self.weight_master
+        if p is not W or not (p.is_cuda and p.dim() == 2 and p.is_contiguous() and g.is_contiguous()
+                              and g.dtype == torch.float32 and m.is_contiguous() and v.is_contiguous()):
+            return False
+        level = self.level
+        wd = _working(level)
+        N, K = W.shape
+        if self._wq_level != level or self._wq is None or self._wq.dtype != wd:
+            return False                  # buffers follow pre_step's allocation
+        if self._wqt is None or self._wqt.dtype != wd:
+            return False
+        want_t = self._needs_wt
+        s = _lib.stream_handle(W.device)
+        lib = _lib.lib()
+        st = lib.apa_adamw_cast(W.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), N, K, W.stride(0), lr, beta1,
+                                beta2, eps, weight_decay, step, self._wq.data_ptr(), _operand_code(level),
+                                self._wq.stride(0), self._wqt.data_ptr() if want_t else None, self._wqt.stride(0),
+                                self._w_pending_opt.data_ptr(), s)
+        if st == _lib.ERR_UNSUPPORTED:
+            return False
+        _lib.check(st, "apa_adamw_cast")
+        self._prerefreshed = True
+        self._prerefresh_key = (level, W._version, W.data_ptr())
+        self._prerefresh_t = want_t
+        return True
 
     def _make_wqt(self) -> None:
         """Transposed working weight for dgrad, made late when pre_step skipped it."""

@@ -266,7 +266,7 @@ def run_ours(args):
     gpt = {}
     for name in args.gpt:
         gpt[name] = run_gpt(torch, dist, name, world, rank, dev, args.gpt_steps, max(4, args.warmup), barrier,
-                            max_over_ranks, graphed=not args.gpt_eager)
+                            max_over_ranks, graphed=not args.gpt_eager, optimizer=args.gpt_optimizer)
     out = None
     if rank == 0:
         fp8 = results["fp8"]
@@ -413,7 +413,8 @@ def gpt_batches(torch, cfgd, rank, device, n=4):
     return out
 
 
-def run_gpt(torch, dist, name, world, rank, dev, steps, warmup, barrier, max_over_ranks, graphed=True):
+def run_gpt(torch, dist, name, world, rank, dev, steps, warmup, barrier, max_over_ranks, graphed=True,
+            optimizer="torch"):
     import torch.nn as nn
     import torch.nn.functional as F
     import apa
@@ -421,7 +422,12 @@ def run_gpt(torch, dist, name, world, rank, dev, steps, warmup, barrier, max_ove
     cfgd = GPT_CONFIGS[name]
     model, cfg = build_gpt(torch, nn, F, apa, cfgd, dev)
     mgr = APAManager(model, cfg)
-    opt = torch.optim.AdamW(mgr.get_trainable_parameters(), lr=cfgd["lr"], weight_decay=0.01, fused=True)
+    if optimizer == "apa":
+        # AdamW with each APALinear weight's next working copy written in the same pass
+        from apa.optim import APAAdamW
+        opt = APAAdamW(mgr, lr=cfgd["lr"], weight_decay=0.01)
+    else:
+        opt = torch.optim.AdamW(mgr.get_trainable_parameters(), lr=cfgd["lr"], weight_decay=0.01, fused=True)
     batches = gpt_batches(torch, cfgd, rank, dev)
     V = cfgd["vocab_pad"]
 
@@ -468,6 +474,8 @@ def run_gpt(torch, dist, name, world, rank, dev, steps, warmup, barrier, max_ove
         levels[m.level] = levels.get(m.level, 0) + 1
     out = {"tokens_per_s": round(tokens / ms * 1e3, 1), "ms_per_step": round(ms, 3), "global_batch_tokens": tokens,
            "mode": "cuda-graph replay of pre_step+fwd+bwd" if graphed else "eager",
+           "optimizer": "APAAdamW (fused weight update + working-copy cast)" if optimizer == "apa"
+           else "torch.optim.AdamW(fused=True)",
            "apa_linear_params": nparam, "levels": {["fp8", "fp16", "tf32"][k]: v for k, v in sorted(levels.items())},
            "loss": round(float(loss.item()), 4)}
     del model, mgr, opt
@@ -823,6 +831,8 @@ def main():
                     help="GPT training workloads also timed (tokens/s), comma-separated; '' for none")
     ap.add_argument("--gpt-steps", type=int, default=10)
     ap.add_argument("--gpt-eager", action="store_true", help="time the GPT workloads without CUDA-graph replay")
+    ap.add_argument("--gpt-optimizer", choices=["torch", "apa"], default="torch",
+                    help="optimizer of the GPT workloads: torch.optim.AdamW(fused) or apa.optim.APAAdamW")
     ap.add_argument("--eager", action="store_true",
                     help="time the APALinear steps without CUDA-graph replay (every launch from the host)")
     ap.add_argument("--profile-case", default=None,

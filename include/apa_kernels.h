@@ -217,6 +217,22 @@ int apa_gemm_plan(int rung, int epilogue, int64_t M, int64_t N, int64_t K, int o
                   int grid_cap, int* tile_out, int* epi_warps_out);
 
 /*
+ * AdamW on an fp32 master weight [rows, cols] (row pitch ld, shared by p, g,
+ * m, v) fused with the next step's working copy: p, m, v updated in place in
+ * torch.optim.AdamW's order of operations (decoupled decay, bias-corrected
+ * step `step` >= 1) and, in the same pass, the updated p cast to work_dtype
+ * (E4M3, F16 or TF32) into wq and/or its transpose wq_t, with max |cast
+ * value| written to *w_amax (which is reset first). APA_ERR_UNSUPPORTED for layouts the streaming
+ * cast does not take (rows must be 16-byte aligned). Replaces the optimizer
+ * step plus the weight half of the working-copy refresh in pre_step
+ * (manager.py:145-172, layers.py:368-372).
+ */
+int apa_adamw_cast(float* p, const float* g, float* m, float* v, int64_t rows, int64_t cols, int64_t ld,
+                   float lr, float beta1, float beta2, float eps, float weight_decay, int64_t step,
+                   void* wq, int work_dtype, int64_t ld_q, void* wq_t, int64_t ld_qt, float* w_amax,
+                   void* stream);
+
+/*
  * Forensic statistics of a flat tensor of n elements (n < 2^32) into a
  * 5-word device record (zeroed here): [0] (max |x| fp32 bits << 32) | ~index
  * of its first occurrence (NaN ranks largest), [1] sum and [2] sum of squares
