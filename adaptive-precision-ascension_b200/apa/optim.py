@@ -38,10 +38,13 @@ class APAAdamW(torch.optim.Optimizer):
         self._owner: Dict[int, object] = {id(m.weight_master): m for m in manager.apa_modules.values()}
         self.fused_steps = 0        # weight updates done by the fused kernel (for tests and reports)
 
-    def _state(self, p):
+    def _state(self, p, fused_weight: bool):
         st = self.state[p]
         if not st:
-            st["step"] = torch.zeros((), dtype=torch.float32)
+            # the fused weight kernel counts steps on the host; every other
+            # parameter goes through torch's fused AdamW, which wants its step
+            # counter on the parameter's device
+            st["step"] = torch.zeros((), dtype=torch.float32, device="cpu" if fused_weight else p.device)
             st["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
             st["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
         return st
@@ -60,22 +63,25 @@ class APAAdamW(torch.optim.Optimizer):
             for p in group["params"]:
                 if p.grad is None:
                     continue
-                st = self._state(p)
                 mod = self._owner.get(id(p))
+                st = self._state(p, mod is not None)
                 if mod is not None:
-                    n = st.get("fused_step", int(st["step"].item())) + 1
+                    n = (st["fused_step"] if "fused_step" in st else int(st["step"].item())) + 1
                     if mod._adamw_refresh(p, p.grad, st["exp_avg"], st["exp_avg_sq"], lr, beta1, beta2, eps, wd, n):
                         st["fused_step"] = n
                         st["step"].fill_(n)
                         self.fused_steps += 1
                         continue
                     st.pop("fused_step", None)   # the regular path counts the step itself
+                if p.is_cuda and st["step"].device != p.device:
+                    st["step"] = st["step"].to(p.device)
                 rest[0].append(p)
                 rest[1].append(p.grad)
                 rest[2].append(st["exp_avg"])
                 rest[3].append(st["exp_avg_sq"])
                 rest[4].append(st["step"])
             if rest[0]:
-                _torch_adamw.adamw(rest[0], rest[1], rest[2], rest[3], [], rest[4], amsgrad=False, beta1=beta1,
-                                   beta2=beta2, lr=lr, weight_decay=wd, eps=eps, maximize=False)
+                fused = all(t.is_cuda and t.dtype == torch.float32 for t in rest[0]) or None
+                _torch_adamw.adamw(rest[0], rest[1], rest[2], rest[3], [], rest[4], fused=fused, amsgrad=False,
+                                   beta1=beta1, beta2=beta2, lr=lr, weight_decay=wd, eps=eps, maximize=False)
         return loss

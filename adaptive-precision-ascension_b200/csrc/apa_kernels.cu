@@ -7,3 +7,4 @@
 #include "ladder.cu"
 #include "noalloc.cu"
 #include "forensic.cu"
+#include "adamw.cu"

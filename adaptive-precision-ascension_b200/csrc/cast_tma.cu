@@ -141,26 +141,10 @@ struct TmaCastArgs {
   int telem_on_source;
   int has_dst, has_dst_t;
   int tf32;                 // fp32 destination: stored values rounded to the TF32 grid
-  // AdamW prologue (fp32 source = the master weight): the tile of p is
-  // updated with g, m, v (same [rows, cols] layout, row pitch ld) before it is
-  // cast; p, m, v are written back
-  int adam;
-  float* p_out; const float* g; float* m; float* v; int64_t ld;
-  float decay, one_m_b1, b2, one_m_b2, eps, step_size, bc2_sqrt;
 };
 
-// One AdamW update in the order of torch.optim.AdamW (decoupled decay,
-// lerp of the first moment, second moment, bias-corrected step).
-__device__ __forceinline__ float adamw_elem(float pv, float g, float& m, float& v, const TmaCastArgs& a) {
-  pv = __fmul_rn(pv, a.decay);
-  m = __fadd_rn(m, __fmul_rn(a.one_m_b1, __fsub_rn(g, m)));
-  v = __fadd_rn(__fmul_rn(v, a.b2), __fmul_rn(__fmul_rn(g, g), a.one_m_b2));
-  const float denom = __fadd_rn(__fdiv_rn(__fsqrt_rn(v), a.bc2_sqrt), a.eps);
-  return __fadd_rn(pv, __fmul_rn(-a.step_size, __fdiv_rn(m, denom)));
-}
-
-template <int SRC, int DST, bool ADAM = false>
-__global__ void __launch_bounds__(kCastTmaThreads, (DST == APA_DT_F32 || ADAM) ? 1 : 2)
+template <int SRC, int DST>
+__global__ void __launch_bounds__(kCastTmaThreads, DST == APA_DT_F32 ? 1 : 2)
     cast_tma_kernel(const __grid_constant__ CUtensorMap tmS, const __grid_constant__ CUtensorMap tmD,
                     const __grid_constant__ CUtensorMap tmT, TmaCastArgs p) {
   using C = TcCfg<SRC, DST>;
@@ -270,63 +254,6 @@ __global__ void __launch_bounds__(kCastTmaThreads, (DST == APA_DT_F32 || ADAM) ?
           const float4 lo = f ? b : a, hi = f ? a : b;
           v[r][0] = lo.x; v[r][1] = lo.y; v[r][2] = lo.z; v[r][3] = lo.w;
           v[r][4] = hi.x; v[r][5] = hi.y; v[r][6] = hi.z; v[r][7] = hi.w;
-        }
-      }
-      if constexpr (SRC == APA_DT_F32 && ADAM) {
-        // rows in two batches of four: all g, m, v loads of a batch are in
-        // flight together (the load latency, not bandwidth, bounds one row)
-        const int64_t col = tc * kCTC + 8 * bj;
-        const bool col_full = col + 8 <= p.cols;
-#pragma unroll
-        for (int rb = 0; rb < 8; rb += 4) {
-          float gg[4][8], mm[4][8], vv[4][8];
-#pragma unroll
-          for (int r4 = 0; r4 < 4; ++r4) {
-            const int64_t row = tr * kCTR + 8 * bi + rb + r4;
-            if (row < p.rows && col_full) {
-              const int64_t off = row * p.ld + col;
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const float4 g4 = *reinterpret_cast<const float4*>(p.g + off + 4 * h);
-                const float4 m4 = *reinterpret_cast<const float4*>(p.m + off + 4 * h);
-                const float4 v4 = *reinterpret_cast<const float4*>(p.v + off + 4 * h);
-                gg[r4][4 * h] = g4.x; gg[r4][4 * h + 1] = g4.y; gg[r4][4 * h + 2] = g4.z; gg[r4][4 * h + 3] = g4.w;
-                mm[r4][4 * h] = m4.x; mm[r4][4 * h + 1] = m4.y; mm[r4][4 * h + 2] = m4.z; mm[r4][4 * h + 3] = m4.w;
-                vv[r4][4 * h] = v4.x; vv[r4][4 * h + 1] = v4.y; vv[r4][4 * h + 2] = v4.z; vv[r4][4 * h + 3] = v4.w;
-              }
-            }
-          }
-#pragma unroll
-          for (int r4 = 0; r4 < 4; ++r4) {
-            const int r = rb + r4;
-            const int64_t row = tr * kCTR + 8 * bi + r;
-            if (row >= p.rows || col >= p.cols) continue;
-            const int64_t off = row * p.ld + col;
-            if (col_full) {
-#pragma unroll
-              for (int c = 0; c < 8; ++c) v[r][c] = adamw_elem(v[r][c], gg[r4][c], mm[r4][c], vv[r4][c], p);
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                *reinterpret_cast<float4*>(p.p_out + off + 4 * h) =
-                    make_float4(v[r][4 * h], v[r][4 * h + 1], v[r][4 * h + 2], v[r][4 * h + 3]);
-                *reinterpret_cast<float4*>(p.m + off + 4 * h) =
-                    make_float4(mm[r4][4 * h], mm[r4][4 * h + 1], mm[r4][4 * h + 2], mm[r4][4 * h + 3]);
-                *reinterpret_cast<float4*>(p.v + off + 4 * h) =
-                    make_float4(vv[r4][4 * h], vv[r4][4 * h + 1], vv[r4][4 * h + 2], vv[r4][4 * h + 3]);
-              }
-            } else {
-#pragma unroll
-              for (int c = 0; c < 8; ++c) {
-                if (col + c < p.cols) {
-                  float mc = p.m[off + c], vc = p.v[off + c];
-                  v[r][c] = adamw_elem(v[r][c], p.g[off + c], mc, vc, p);
-                  p.p_out[off + c] = v[r][c];
-                  p.m[off + c] = mc;
-                  p.v[off + c] = vc;
-                }
-              }
-            }
-          }
         }
       }
       uint32_t m = 0;
@@ -563,22 +490,18 @@ bool cast_map(CUtensorMap* tm, CUtensorMapDataType dt, const void* ptr, int64_t 
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-struct AdamArgs {
-  const float* g; float* m; float* v;
-  float decay, one_m_b1, b2, one_m_b2, eps, step_size, bc2_sqrt;
-};
 
-template <int SRC, int DST, bool ADAM = false>
-int launch_cast_tma_t(const CastParams& cp, cudaStream_t s, const AdamArgs* adam = nullptr) {
+template <int SRC, int DST>
+int launch_cast_tma_t(const CastParams& cp, cudaStream_t s) {
   using C = TcCfg<SRC, DST>;
   static std::once_flag once;
   static int blocks_per_sm = 0;
   std::call_once(once, [] {
-    if (cudaFuncSetAttribute(cast_tma_kernel<SRC, DST, ADAM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(cast_tma_kernel<SRC, DST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::kSmemBytes) != cudaSuccess)
       return;
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, cast_tma_kernel<SRC, DST, ADAM>, kCastTmaThreads,
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, cast_tma_kernel<SRC, DST>, kCastTmaThreads,
                                                       C::kSmemBytes) == cudaSuccess)
       blocks_per_sm = n;
   });
@@ -615,19 +538,9 @@ int launch_cast_tma_t(const CastParams& cp, cudaStream_t s, const AdamArgs* adam
   a.colsum = cp.colsum; a.telem_on_source = cp.telem_on_source;
   a.has_dst = cp.dst != nullptr; a.has_dst_t = cp.dst_t != nullptr;
   a.tf32 = cp.tf32;
-  a.adam = 0;
-  a.p_out = nullptr; a.g = nullptr; a.m = nullptr; a.v = nullptr; a.ld = 0;
-  a.decay = a.one_m_b1 = a.b2 = a.one_m_b2 = a.eps = a.step_size = a.bc2_sqrt = 0.0f;
-  if (adam) {
-    a.adam = 1;
-    a.p_out = const_cast<float*>(static_cast<const float*>(cp.src));
-    a.g = adam->g; a.m = adam->m; a.v = adam->v; a.ld = cp.ld_src;
-    a.decay = adam->decay; a.one_m_b1 = adam->one_m_b1; a.b2 = adam->b2; a.one_m_b2 = adam->one_m_b2;
-    a.eps = adam->eps; a.step_size = adam->step_size; a.bc2_sqrt = adam->bc2_sqrt;
-  }
   const int64_t tiles = ((cp.rows + kCTR - 1) / kCTR) * ((cp.cols + kCTC - 1) / kCTC);
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)num_sms() * blocks_per_sm));
-  cast_tma_kernel<SRC, DST, ADAM><<<(unsigned)grid, kCastTmaThreads, C::kSmemBytes, s>>>(ms, md, mt, a);
+  cast_tma_kernel<SRC, DST><<<(unsigned)grid, kCastTmaThreads, C::kSmemBytes, s>>>(ms, md, mt, a);
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }
 
@@ -665,49 +578,3 @@ int cast_tma_try(int src_dt, int dst_dt, const CastParams& p, cudaStream_t s) {
 }
 
 }  // namespace apa
-
-// AdamW on an fp32 master weight fused with the next step's working copy:
-// p, m, v updated in place (torch.optim.AdamW order of operations, step >= 1)
-// and, in the same pass, p cast to the working dtype into wq (row-major)
-// and/or wq_t (transposed) with max |cast value| written to *w_amax. The layouts the streaming cast accepts only (16-byte rows);
-// APA_ERR_UNSUPPORTED otherwise (the caller then runs AdamW and the cast
-// separately).
-extern "C" int apa_adamw_cast(float* p, const float* g, float* m, float* v, int64_t rows, int64_t cols, int64_t ld,
-                              float lr, float beta1, float beta2, float eps, float weight_decay, int64_t step,
-                              void* wq, int work_dtype, int64_t ld_q, void* wq_t, int64_t ld_qt, float* w_amax,
-                              void* stream) {
-  using namespace apa;
-  if (!p || !g || !m || !v || rows <= 0 || cols <= 0 || ld < cols || step < 1) return APA_ERR_INVALID;
-  if (!wq && !wq_t) return APA_ERR_INVALID;
-  const int tf32 = work_dtype == APA_DT_TF32;
-  const int dst = tf32 ? APA_DT_F32 : work_dtype;
-  if (dst != APA_DT_E4M3 && dst != APA_DT_F16 && dst != APA_DT_F32) return APA_ERR_UNSUPPORTED;
-  const int ed = dst == APA_DT_E4M3 ? 1 : dst == APA_DT_F16 ? 2 : 4;
-  if (!tma_ok(p, ld, 4) || !tma_ok(g, ld, 4) || !tma_ok(m, ld, 4) || !tma_ok(v, ld, 4)) return APA_ERR_UNSUPPORTED;
-  if ((wq && !tma_ok(wq, ld_q, ed)) || (wq_t && !tma_ok(wq_t, ld_qt, ed))) return APA_ERR_UNSUPPORTED;
-  if (rows >= (1ll << 31) || cols >= (1ll << 31)) return APA_ERR_UNSUPPORTED;
-  CastParams cp;
-  cp.src = p; cp.rows = rows; cp.cols = cols; cp.ld_src = ld;
-  cp.dst = wq; cp.ld_dst = ld_q; cp.dst_t = wq_t; cp.ld_dst_t = ld_qt;
-  cp.amax = w_amax; cp.flag = nullptr; cp.merge_amax = nullptr; cp.colsum = nullptr;
-  cp.telem_on_source = 0; cp.vec_src = 1; cp.vec_dst = 1; cp.vec_dst_t = 1; cp.tf32 = tf32;
-  AdamArgs ad;
-  ad.g = g; ad.m = m; ad.v = v;
-  const double bc1 = 1.0 - std::pow((double)beta1, (double)step);
-  const double bc2 = 1.0 - std::pow((double)beta2, (double)step);
-  ad.decay = (float)(1.0 - (double)lr * (double)weight_decay);
-  ad.one_m_b1 = (float)(1.0 - (double)beta1);
-  ad.b2 = beta2;
-  ad.one_m_b2 = (float)(1.0 - (double)beta2);
-  ad.eps = eps;
-  ad.step_size = (float)((double)lr / bc1);
-  ad.bc2_sqrt = (float)std::sqrt(bc2);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // the working copy's amax starts over with each update
-  if (w_amax && cudaMemsetAsync(w_amax, 0, sizeof(float), s) != cudaSuccess) return APA_ERR_CUDA;
-  switch (dst) {
-    case APA_DT_E4M3: return launch_cast_tma_t<APA_DT_F32, APA_DT_E4M3, true>(cp, s, &ad);
-    case APA_DT_F16: return launch_cast_tma_t<APA_DT_F32, APA_DT_F16, true>(cp, s, &ad);
-    default: return launch_cast_tma_t<APA_DT_F32, APA_DT_F32, true>(cp, s, &ad);
-  }
-}

@@ -197,6 +197,7 @@ def run_ours(args):
 
     results = {}
     gemm_roof = None
+    optim = None
     launches = 0
     clocks = None
     pk = peaks()
@@ -254,6 +255,7 @@ def run_ours(args):
             results[name]["frac_of_library_gemm"] = FLOPS_STEP / ms / 1e9 / libpk[f"{name}_tflops"]
         if level == 0:
             gemm_roof = time_gemm(torch, _lib, lin, xr, dev, pk, libpk)
+            optim = time_optimizer(torch, _lib, dev, pk)
         # graphs holding NCCL work must be released before the process group
         gstep = step = None
         del lin, mgr
@@ -283,6 +285,7 @@ def run_ours(args):
                       for k, v in results.items()},
             "library_gemm_peaks": libpk,
             "roofline": gemm_roof,
+            "optimizer": optim,
             "e2e": e2e,
             "gpt": gpt,
             "gpu_launches": launches,
@@ -544,6 +547,63 @@ def time_gemm(torch, _lib, lin, xr, dev, pk, libpk):
             # dram__bytes_read.sum + dram__bytes_write.sum of this kernel from one ncu
             # capture (profiles/gemm_fp8_fwd_8192x4096x4096.md), bytes per launch
             "traffic": 145.9e6}
+
+
+def time_optimizer(torch, _lib, dev, pk):
+    """AdamW on the 4096x4096 master weight fused with its next FP8 working
+    copies (apa_adamw_cast: p, m, v updated, W_q and W_q^T written, weight
+    amax), against torch.optim.AdamW(fused=True) followed by the library's
+    cast of the updated weight. CUDA events on the launching stream; every
+    launch streams about 0.5 GB, four times the L2."""
+    lib = _lib.lib()
+    st = _lib.stream_handle(dev)
+    s = torch.cuda.current_stream(dev)
+    g0 = torch.Generator(device=dev).manual_seed(5)
+    p = torch.randn(N, K, device=dev, generator=g0) * 0.02
+    g = torch.randn(N, K, device=dev, generator=g0) * 1e-3
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    wq = torch.empty(N, K, dtype=torch.float8_e4m3fn, device=dev)
+    wqt = torch.empty(K, N, dtype=torch.float8_e4m3fn, device=dev)
+    amax = torch.zeros(1, device=dev)
+    pt = p.clone().requires_grad_(True)
+    pt.grad = g.clone()
+    opt = torch.optim.AdamW([pt], lr=1e-3, weight_decay=0.01, fused=True)
+    n = [0]
+
+    def fused():
+        n[0] += 1
+        _lib.check(lib.apa_adamw_cast(p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), N, K, K, 1e-3, 0.9,
+                                      0.999, 1e-8, 0.01, n[0], wq.data_ptr(), _lib.DT_E4M3, K, wqt.data_ptr(), N,
+                                      amax.data_ptr(), st), "adamw_cast")
+
+    def separate():
+        opt.step()
+        _lib.check(lib.apa_cast(pt.data_ptr(), _lib.DT_F32, N, K, K, wq.data_ptr(), _lib.DT_E4M3, K, wqt.data_ptr(),
+                                N, amax.data_ptr(), None, 0, None, None, st), "cast")
+
+    def timed(fn, reps=20):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(reps):
+            fn()
+        e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps * 1e3
+
+    t_f, t_s = [], []
+    for _ in range(2):
+        t_f.append(timed(fused))
+        t_s.append(timed(separate))
+    tf, ts = min(t_f), min(t_s)
+    # algorithmic bytes: read p, g, m, v (fp32), write p, m, v (fp32) and the two E4M3 copies
+    nbytes = N * K * (7 * 4 + 2)
+    gbs = nbytes / (tf * 1e-6) / 1e9
+    return {"kernel": "adamw_cast_kernel E4M3, 4096x4096 fp32 master", "bound": "hbm",
+            "us_per_launch": round(tf, 2), "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+            "frac": round(gbs / pk["hbm_gbs"], 4), "bytes_per_launch": nbytes,
+            "torch_adamw_fused_plus_cast_us": round(ts, 2), "speedup": round(ts / tf, 3)}
 
 
 def run_e2e(torch, make, x, dy32, dev, args, world, barrier, max_over_ranks):
@@ -813,6 +873,18 @@ def profile_case(case: str):
         step(4)
         torch.cuda.synchronize()
         torch.cuda.cudart().cudaProfilerStop()
+    elif case == "adamw-fp8":
+        # AdamW on the 4096x4096 master fused with its FP8 working copies
+        p = torch.randn(N, K, device=dev, generator=g) * 0.02
+        gr = torch.randn(N, K, device=dev, generator=g) * 1e-3
+        m, v = torch.zeros_like(p), torch.zeros_like(p)
+        wq = torch.empty(N, K, dtype=torch.float8_e4m3fn, device=dev)
+        wqt = torch.empty(K, N, dtype=torch.float8_e4m3fn, device=dev)
+        amax = torch.zeros(1, device=dev)
+        for i in range(3):
+            _lib.check(lib.apa_adamw_cast(p.data_ptr(), gr.data_ptr(), m.data_ptr(), v.data_ptr(), N, K, K, 1e-3,
+                                          0.9, 0.999, 1e-8, 0.01, i + 1, wq.data_ptr(), _lib.DT_E4M3, K,
+                                          wqt.data_ptr(), N, amax.data_ptr(), st), "adamw_cast")
     else:
         raise SystemExit(f"unknown profile case {case}")
     torch.cuda.synchronize()

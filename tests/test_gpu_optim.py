@@ -29,8 +29,9 @@ def bits(t):
 
 
 @pytest.mark.parametrize("rung", [0, 1, 2])
-@pytest.mark.parametrize("shape", [(128, 64), (200, 136), (1024, 512)])
-def test_adamw_cast_kernel(L, rung, shape):
+@pytest.mark.parametrize("copies", ["both", "row", "transposed"])
+@pytest.mark.parametrize("shape", [(128, 64), (200, 136), (33, 20), (1024, 512), (4096, 1024)])
+def test_adamw_cast_kernel(L, rung, copies, shape):
     N, K = shape
     g0 = torch.Generator(device="cuda").manual_seed(N * 7 + rung)
     p = (torch.randn(N, K, device="cuda", generator=g0) * 0.05).contiguous()
@@ -45,7 +46,10 @@ def test_adamw_cast_kernel(L, rung, shape):
         ld = (cols * es + 15) // 16 * 16 // es
         return torch.empty(rows, ld, dtype=wdt, device="cuda")[:, :cols]
 
+    if copies != "both" and shape not in ((200, 136), (1024, 512)):
+        pytest.skip("one copy: two shapes suffice")
     wq, wqt = alloc(N, K), alloc(K, N)
+    want_q, want_t = copies != "transposed", copies != "row"
     amax = torch.zeros(1, device="cuda")
     s = L.stream_handle()
     for step in range(1, 4):
@@ -54,8 +58,9 @@ def test_adamw_cast_kernel(L, rung, shape):
         opt.step()
         amax.zero_()
         L.check(L.lib().apa_adamw_cast(p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), N, K, K, 3e-3, 0.9,
-                                       0.95, 1e-8, 0.1, step, wq.data_ptr(), code, wq.stride(0), wqt.data_ptr(),
-                                       wqt.stride(0), amax.data_ptr(), s), "apa_adamw_cast")
+                                       0.95, 1e-8, 0.1, step, wq.data_ptr() if want_q else None, code, wq.stride(0),
+                                       wqt.data_ptr() if want_t else None, wqt.stride(0), amax.data_ptr(), s),
+                "apa_adamw_cast")
         torch.cuda.synchronize()
         st = opt.state[ref]
         for got, want in ((p, ref.detach()), (m, st["exp_avg"]), (v, st["exp_avg_sq"])):
@@ -67,8 +72,10 @@ def test_adamw_cast_kernel(L, rung, shape):
         L.check(L.lib().apa_cast(p.data_ptr(), L.DT_F32, N, K, K, cq.data_ptr(), code, cq.stride(0), cqt.data_ptr(),
                                  cqt.stride(0), camax.data_ptr(), None, 0, None, None, s), "apa_cast")
         torch.cuda.synchronize()
-        assert torch.equal(bits(wq.contiguous()), bits(cq.contiguous()))
-        assert torch.equal(bits(wqt.contiguous()), bits(cqt.contiguous()))
+        if want_q:
+            assert torch.equal(bits(wq.contiguous()), bits(cq.contiguous()))
+        if want_t:
+            assert torch.equal(bits(wqt.contiguous()), bits(cqt.contiguous()))
         assert amax.item() == camax.item()
     assert L.device_status() == 0
 
