@@ -10,6 +10,18 @@ buffers that NCCL reduces, with no packing copies. A bucket's all-reduce is
 issued (asynchronously, on the process group's stream) as soon as all of its
 gradients are written, and buckets are issued in a fixed order so every rank
 runs the same collectives in the same sequence.
+
+Optionally (``block_bytes`` > 0; off by default) large APALinear weights sit
+alone in their bucket and are reduced in row blocks: the layer's backward
+computes the weight gradient one block of output rows at a time
+(``apa_linear_wgrad_block``) and the block's all-reduce starts as soon as its
+rows are written, while the next block and the input-gradient GEMM run. A
+block holds as many 256-row tile rows as one wave of the GEMMs (on the SMs
+left beside the collective) covers. Results are bit-identical to the
+whole-bucket reduction; on two B200s the single-layer 8192x4096x4096 step was
+slower with blocks (0.60-0.66 ms against 0.56 ms for 1024- and 2048-row
+blocks, with and without SM reserves or a CTA-capped communicator), so the
+whole-bucket reduction overlapping the input-gradient GEMM stays the default.
 """
 from __future__ import annotations
 
@@ -30,7 +42,9 @@ class _Bucket:
             self.views[id(p)] = self.flat[off:off + p.numel()].view_as(p)
             off += p.numel()
         self.pending = len(params)
-        self.handle = None
+        self.handles = []
+        self.blocks = None            # row blocks of a single large weight, reduced as they finish
+        self.blocks_issued = False
 
 
 # SMs left to the collective's kernel while a bucket all-reduce is in flight:
@@ -54,7 +68,7 @@ def _capped_nccl_group(process_group, max_ctas: int):
 
 class GradientAverager:
     def __init__(self, mgr, process_group=None, bucket_bytes: int = 64 << 20, reserved_sms: int = RESERVED_SMS,
-                 max_ctas: int = 0):
+                 max_ctas: int = 0, block_bytes: int = 0, block_rows: int = 0):
         self.world = dist.get_world_size(process_group)
         if max_ctas > 0 and dist.get_backend(process_group) == "nccl":
             process_group = _capped_nccl_group(process_group, max_ctas)
@@ -74,9 +88,26 @@ class GradientAverager:
                 seen.add(id(p))
         params = list(reversed(params))
         device = params[0].device if params else torch.device("cpu")
+        owner = {id(m.weight_master): m for m in mgr.apa_modules.values()}
+        blocked = {}
+        if block_bytes > 0:
+            for p in params:
+                m = owner.get(id(p))
+                if m is not None and p.dim() == 2 and p.numel() * 4 >= block_bytes:
+                    blocks = self._row_blocks(p, reserved_sms, block_rows)
+                    if len(blocks) >= 2:
+                        blocked[id(p)] = (m, blocks)
         self.buckets: List[_Bucket] = []
         cur, cur_bytes = [], 0
         for p in params:
+            if id(p) in blocked:
+                if cur:
+                    self.buckets.append(_Bucket(cur, device))
+                    cur, cur_bytes = [], 0
+                b = _Bucket([p], device)
+                b.blocks = blocked[id(p)][1]
+                self.buckets.append(b)
+                continue
             cur.append(p)
             cur_bytes += p.numel() * 4
             if cur_bytes >= bucket_bytes:
@@ -99,6 +130,7 @@ class GradientAverager:
         apa_params = set()
         for m in mgr.apa_modules.values():
             m._grad_ready_cb = self._apa_ready
+            m._dp = self
             apa_params.add(id(m.weight_master))
             if m.bias_master is not None:
                 apa_params.add(id(m.bias_master))
@@ -107,6 +139,19 @@ class GradientAverager:
             for p in b.params:
                 if id(p) not in apa_params:
                     self._hooks.append(p.register_post_accumulate_grad_hook(self._param_ready))
+
+    @staticmethod
+    def _row_blocks(p, reserved_sms: int, block_rows: int):
+        """Row blocks [r0, r1) of a weight gradient [N, K]: whole 256-row tile
+        rows, as many as one wave of 256x256 tiles covers on the SMs left
+        beside the collective (block_rows overrides)."""
+        N, K = p.shape
+        rows = block_rows
+        if rows <= 0:
+            sms = torch.cuda.get_device_properties(p.device).multi_processor_count if p.is_cuda else 148
+            clusters = max(1, (sms - max(0, reserved_sms)) // 2)
+            rows = 256 * max(1, clusters // max(1, (K + 255) // 256))
+        return [(r, min(N, r + rows)) for r in range(0, N, rows)]
 
     # grads are views into the buckets; re-attach after zero_grad(set_to_none)
     def arm(self):
@@ -117,7 +162,8 @@ class GradientAverager:
                 if p.grad is None or p.grad.data_ptr() != v.data_ptr():
                     p.grad = v
             b.pending = len(b.params)
-            b.handle = None
+            b.handles = []
+            b.blocks_issued = False
         self.next = 0
         self.ready_count = 0
         self.launch_marks = []
@@ -149,26 +195,59 @@ class GradientAverager:
                         - self.reserved_sms)
             _lib.check(_lib.lib().apa_set_gemm_sm_limit(n), "apa_set_gemm_sm_limit")
 
-    def _launch(self, b: _Bucket):
-        self.launch_marks.append(self.ready_count)
+    def _all_reduce(self, b: _Bucket, t: torch.Tensor):
         if not self.limited:
             self._limit_gemms(True)
             self.limited = True
         op = self.avg_op if self.avg_op is not None else dist.ReduceOp.SUM
-        if b.flat.is_cuda and torch.cuda.is_current_stream_capturing():
+        if t.is_cuda and torch.cuda.is_current_stream_capturing():
             # inside a CUDA-graph capture: the reduction runs on a stream forked
             # from the capture stream, so the graph runs it alongside the
             # kernels captured after it; join_capture() joins the fork at the end
-            cur = torch.cuda.current_stream(b.flat.device)
+            cur = torch.cuda.current_stream(t.device)
             if self.comm_stream is None:
-                self.comm_stream = torch.cuda.Stream(device=b.flat.device)
+                self.comm_stream = torch.cuda.Stream(device=t.device)
             self.comm_stream.wait_stream(cur)
             with torch.cuda.stream(self.comm_stream):
-                dist.all_reduce(b.flat, op=op, group=self.pg)
+                dist.all_reduce(t, op=op, group=self.pg)
             self.capture_fork = True
-            b.handle = None
         else:
-            b.handle = dist.all_reduce(b.flat, op=op, group=self.pg, async_op=True)
+            b.handles.append(dist.all_reduce(t, op=op, group=self.pg, async_op=True))
+
+    def _launch(self, b: _Bucket):
+        self.launch_marks.append(self.ready_count)
+        if b.blocks_issued:
+            return                    # its row blocks went out during the backward
+        self._all_reduce(b, b.flat)
+
+    def grad_view(self, p):
+        """p's view into its bucket while a step is armed (for a backward that
+        finds p.grad cleared after pre_step), else None."""
+        bi = self.where.get(id(p))
+        if not self.armed or bi is None:
+            return None
+        return self.buckets[bi].views[id(p)]
+
+    # row-block reduction of a large APALinear weight (called by its backward)
+    def weight_blocks(self, mod, g):
+        """The row blocks in which mod's weight gradient is to be computed this
+        step, or None: only while armed, with the gradient being the bucket's
+        own view and none of its blocks issued yet."""
+        W = mod.weight_master
+        bi = self.where.get(id(W))
+        if not self.armed or bi is None:
+            return None
+        b = self.buckets[bi]
+        if b.blocks is None or b.blocks_issued or g.data_ptr() != b.views[id(W)].data_ptr():
+            return None
+        return b.blocks
+
+    def weight_block_done(self, mod, r0: int, r1: int):
+        """Rows [r0, r1) of mod's weight gradient are written: reduce them."""
+        W = mod.weight_master
+        b = self.buckets[self.where[id(W)]]
+        b.blocks_issued = True
+        self._all_reduce(b, b.views[id(W)][r0:r1])
 
     def join_capture(self, stream):
         """End of a graph capture: the capture stream waits for the forked
@@ -208,8 +287,8 @@ class GradientAverager:
             return
         self.issue_remaining()
         for b in self.buckets:
-            if b.handle is not None:
-                b.handle.wait()
+            for h in b.handles:
+                h.wait()
             if self.avg_op is None:
                 b.flat.div_(self.world)
             for p in b.params:

@@ -281,20 +281,36 @@ class _APALinearFn(torch.autograd.Function):
         mod._grad_epoch = mod._epoch
         # weight and bias gradients first: in data-parallel runs their bucket
         # all-reduce then overlaps the input-gradient GEMM below
+        dp = mod._dp
         if need_dw:
             W = mod.weight_master
             g = W.grad
-            accumulate = 1
-            if g is None or first:
+            accumulate = 0 if (g is None or first) else 1
+            if g is None:
+                # data parallel: the bucket's view even when the caller cleared
+                # the gradients after pre_step
+                g = dp.grad_view(W) if dp is not None else None
                 if g is None:
                     g = torch.empty_like(W)
-                accumulate = 0
             # small weight gradients over long token counts are split along the
             # tokens (two kernels, fp32 partial sums in a scratch buffer)
             nbytes = ctypes.c_int64(0)
             _lib.check(lib.apa_wgrad_workspace_bytes(level, M, N, K, ctypes.addressof(nbytes)),
                        "apa_wgrad_workspace_bytes")
-            if nbytes.value > 0:
+            blocks = dp.weight_blocks(mod, g) if (dp is not None and nbytes.value == 0 and not accumulate) else None
+            if blocks:
+                # data parallel: rows of the gradient in blocks, each block's
+                # all-reduce issued as soon as its rows are written
+                es = dyqt.element_size()
+                for i, (r0, r1) in enumerate(blocks):
+                    st = lib.apa_linear_wgrad_block(level, dyqt.data_ptr() + r0 * dyqt.stride(0) * es,
+                                                    dyqt.stride(0), ctx.xqt.data_ptr(), ctx.xqt.stride(0),
+                                                    g.data_ptr() + r0 * g.stride(0) * 4, g.stride(0), M, r1 - r0, K,
+                                                    0, mod._uf_counters.data_ptr(),
+                                                    mod.gpu_underflow_ratio.data_ptr(), int(i == len(blocks) - 1), s)
+                    _lib.check(st, "apa_linear_wgrad_block")
+                    dp.weight_block_done(mod, r0, r1)
+            elif nbytes.value > 0:
                 ws = torch.empty(nbytes.value, dtype=torch.uint8, device=g.device)
                 st = lib.apa_linear_wgrad_ws(level, dyqt.data_ptr(), dyqt.stride(0), ctx.xqt.data_ptr(),
                                              ctx.xqt.stride(0), g.data_ptr(), K, M, N, K, accumulate,
@@ -313,11 +329,11 @@ class _APALinearFn(torch.autograd.Function):
         if need_db:
             b = mod.bias_master
             g = b.grad
-            accumulate = 1
-            if g is None or first:
+            accumulate = 0 if (g is None or first) else 1
+            if g is None:
+                g = dp.grad_view(b) if dp is not None else None
                 if g is None:
                     g = torch.empty_like(b)
-                accumulate = 0
             st = lib.apa_colsum_finalize(partial.data_ptr(), nparts, N, _lib.dt_code(wd), g.data_ptr(),
                                          accumulate, s)
             _lib.check(st, "apa_colsum_finalize")
@@ -406,6 +422,7 @@ class APALinear(nn.Module):
         self._epoch = 0
         self._grad_epoch = -1
         self._grad_ready_cb = None
+        self._dp = None                   # data-parallel gradient averager (buckets, row blocks)
         self._register_load_state_dict_pre_hook(_drop_working_copy_keys)
         self.reset_parameters()
         if dev.type != "cpu":

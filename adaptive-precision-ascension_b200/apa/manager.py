@@ -89,7 +89,7 @@ class _LadderState:
 class APAManager:
     def __init__(self, model: nn.Module, config: APAConfig = APAConfig(), process_group=None,
                  sync_gradients: bool = True, bucket_bytes: int = 64 << 20, dp_reserved_sms: int = 16,
-                 dp_max_ctas: int = 0):
+                 dp_max_ctas: int = 0, dp_block_bytes: int = 0, dp_block_rows: int = 0):
         self.model = model
         self.config = config
         self.step_count = 0
@@ -111,6 +111,8 @@ class APAManager:
         self._bucket_bytes = bucket_bytes
         self._dp_reserved_sms = dp_reserved_sms   # SMs the GEMMs leave free while a reduction runs
         self._dp_max_ctas = dp_max_ctas           # >0: gradient communicator capped at this many CTAs
+        self._dp_block_bytes = dp_block_bytes     # weights this large are reduced in row blocks (0: never)
+        self._dp_block_rows = dp_block_rows       # rows per block (0: one GEMM wave)
         self._dp = None
 
     # ------------------------------------------------------------------
@@ -429,7 +431,7 @@ class APAManager:
         from .dp import GradientAverager
         if self._dp is None:
             self._dp = GradientAverager(self, self._pg, self._bucket_bytes, self._dp_reserved_sms,
-                                        self._dp_max_ctas)
+                                        self._dp_max_ctas, self._dp_block_bytes, self._dp_block_rows)
         return self._dp
 
     def _allreduce_grads(self):

@@ -112,6 +112,7 @@ struct EpiArgs {
   float* ratio_max;                 // WGRAD: module gpu_underflow_ratio
   float vmin;                       // WGRAD: underflow threshold as fp32
   int accumulate;                   // WGRAD: add into out instead of overwriting
+  int finalize;                     // WGRAD: form the ratio from the counts (0: leave them for a later block)
   int telem;                        // 0: no telemetry buffers, skip the telemetry-only work
   int splits;                       // split-K: K blocks divided into this many units per tile
   int kb_per_split;                 // 128-byte K slabs per split
@@ -867,16 +868,18 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
         const unsigned long long ticket = atomicAdd(&ea.counters[2], 1ull);
         if (ticket == (unsigned long long)gridDim.x - 1ull) {
           __threadfence();
-          const unsigned long long nzc = atomicAdd(&ea.counters[0], 0ull);
-          const unsigned long long ufc = atomicAdd(&ea.counters[1], 0ull);
-          float ratio = 0.0f;
-          if (nzc != 0ull) ratio = __fdiv_rn(__ull2float_rn(ufc), __ull2float_rn(nzc));
-          if (ea.ratio_max) {
-            const float old = *ea.ratio_max;
-            *ea.ratio_max = (old != old) ? old : fmaxf(old, ratio);
+          if (ea.finalize) {
+            const unsigned long long nzc = atomicAdd(&ea.counters[0], 0ull);
+            const unsigned long long ufc = atomicAdd(&ea.counters[1], 0ull);
+            float ratio = 0.0f;
+            if (nzc != 0ull) ratio = __fdiv_rn(__ull2float_rn(ufc), __ull2float_rn(nzc));
+            if (ea.ratio_max) {
+              const float old = *ea.ratio_max;
+              *ea.ratio_max = (old != old) ? old : fmaxf(old, ratio);
+            }
+            ea.counters[0] = 0ull;
+            ea.counters[1] = 0ull;
           }
-          ea.counters[0] = 0ull;
-          ea.counters[1] = 0ull;
           ea.counters[2] = 0ull;
         }
       }
@@ -1270,7 +1273,7 @@ EpiArgs blank(int64_t M, int64_t N, int64_t K) {
   EpiArgs ea;
   ea.out = nullptr; ea.ldo = 0; ea.out_dt = APA_DT_F32; ea.vec_out = 0; ea.tma_out = 0; ea.coalesced_out = 0;
   ea.bias = nullptr; ea.amax = nullptr; ea.flag = nullptr;
-  ea.counters = nullptr; ea.ratio_max = nullptr; ea.vmin = 0.0f; ea.accumulate = 0; ea.telem = 0;
+  ea.counters = nullptr; ea.ratio_max = nullptr; ea.vmin = 0.0f; ea.accumulate = 0; ea.finalize = 1; ea.telem = 0;
   ea.splits = 1; ea.kb_per_split = 0; ea.split_rows = 0;
   ea.M = (int)M; ea.N = (int)N; ea.K = (int)K;
   return ea;
@@ -1323,6 +1326,23 @@ extern "C" int apa_linear_wgrad(int rung, const void* dyqt, int64_t lddyt, const
   EpiArgs ea = blank(N, K, M);
   ea.out = dw; ea.ldo = lddw; ea.out_dt = APA_DT_F32; ea.vec_out = out_vec(dw, lddw, 4);
   ea.accumulate = accumulate; ea.counters = counters; ea.ratio_max = ratio_max;
+  ea.telem = counters ? 1 : 0;
+  ea.vmin = rung == APA_RUNG_FP8 ? 0.015625f : rung == APA_RUNG_FP16 ? 6.1035e-5f : 0.0f;
+  return apa::gemm_dispatch(rung, apa::gemm::EPI_WGRAD, dyqt, lddyt, xqt, ldxt, ea, 0, 0,
+                            static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int apa_linear_wgrad_block(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt,
+                                      float* dw, int64_t lddw, int64_t M, int64_t rows, int64_t K, int accumulate,
+                                      unsigned long long* counters, float* ratio_max, int last, void* stream) {
+  // rows [r0, r0 + rows) of dw[N, K]: dyqt and dw point at row r0 of dyq^T and dw
+  if (int st = check_dims(rows, K, M)) return st;
+  if (!dyqt || !xqt || !dw || lddw < K || lddyt < M || ldxt < M) return APA_ERR_INVALID;
+  if (rung != APA_RUNG_TF32 && !counters) return APA_ERR_INVALID;
+  EpiArgs ea = blank(rows, K, M);
+  ea.out = dw; ea.ldo = lddw; ea.out_dt = APA_DT_F32; ea.vec_out = out_vec(dw, lddw, 4);
+  ea.accumulate = accumulate; ea.counters = counters; ea.ratio_max = ratio_max;
+  ea.finalize = last ? 1 : 0;
   ea.telem = counters ? 1 : 0;
   ea.vmin = rung == APA_RUNG_FP8 ? 0.015625f : rung == APA_RUNG_FP16 ? 6.1035e-5f : 0.0f;
   return apa::gemm_dispatch(rung, apa::gemm::EPI_WGRAD, dyqt, lddyt, xqt, ldxt, ea, 0, 0,

@@ -192,7 +192,7 @@ def run_ours(args):
         torch.manual_seed(0)
         lin = APALinear(K, N, config=cfg)
         lin.level = level
-        mgr = APAManager(nn.Sequential(lin), cfg)
+        mgr = APAManager(nn.Sequential(lin), cfg, dp_block_bytes=args.dp_block_bytes)
         return lin, mgr
 
     results = {}
@@ -268,7 +268,8 @@ def run_ours(args):
     gpt = {}
     for name in args.gpt:
         gpt[name] = run_gpt(torch, dist, name, world, rank, dev, args.gpt_steps, max(4, args.warmup), barrier,
-                            max_over_ranks, graphed=not args.gpt_eager, optimizer=args.gpt_optimizer)
+                            max_over_ranks, graphed=not args.gpt_eager, optimizer=args.gpt_optimizer,
+                            dp_block_bytes=args.dp_block_bytes)
     out = None
     if rank == 0:
         fp8 = results["fp8"]
@@ -278,7 +279,9 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3",
             "data": "synthetic", "config": dict(CONFIG, parallelism=f"dp{world}",
                                                 launch="eager" if args.eager else
-                                                "cuda-graph replay of pre_step+fwd+bwd, ladder eager"),
+                                                "cuda-graph replay of pre_step+fwd+bwd, ladder eager",
+                                                grad_allreduce=(f"row blocks for weights >= {args.dp_block_bytes} B"
+                                                                if args.dp_block_bytes > 0 else "whole buckets")),
             "rungs": {k: {"tflops": round(v["tflops"], 2), "ms_per_step": round(v["ms_per_step"], 4),
                           "frac_of_peak": round(v["frac_of_peak"], 4),
                           "frac_of_library_gemm": round(v.get("frac_of_library_gemm", 0.0), 4)}
@@ -417,14 +420,14 @@ def gpt_batches(torch, cfgd, rank, device, n=4):
 
 
 def run_gpt(torch, dist, name, world, rank, dev, steps, warmup, barrier, max_over_ranks, graphed=True,
-            optimizer="torch"):
+            optimizer="torch", dp_block_bytes=0):
     import torch.nn as nn
     import torch.nn.functional as F
     import apa
     from apa import APAManager
     cfgd = GPT_CONFIGS[name]
     model, cfg = build_gpt(torch, nn, F, apa, cfgd, dev)
-    mgr = APAManager(model, cfg)
+    mgr = APAManager(model, cfg, dp_block_bytes=dp_block_bytes)
     if optimizer == "apa":
         # AdamW with each APALinear weight's next working copy written in the same pass
         from apa.optim import APAAdamW
@@ -905,6 +908,10 @@ def main():
     ap.add_argument("--gpt-eager", action="store_true", help="time the GPT workloads without CUDA-graph replay")
     ap.add_argument("--gpt-optimizer", choices=["torch", "apa"], default="torch",
                     help="optimizer of the GPT workloads: torch.optim.AdamW(fused) or apa.optim.APAAdamW")
+    ap.add_argument("--dp-block-bytes", type=int, default=0,
+                    help="data parallel: APALinear weights this large have their gradient computed and all-reduced "
+                         "in row blocks (0, the default: one all-reduce per bucket after the whole gradient; "
+                         "row blocks measured slower on 2 GPUs)")
     ap.add_argument("--eager", action="store_true",
                     help="time the APALinear steps without CUDA-graph replay (every launch from the host)")
     ap.add_argument("--profile-case", default=None,

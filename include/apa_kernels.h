@@ -158,6 +158,19 @@ int apa_linear_wgrad(int rung, const void* dyqt, int64_t lddyt, const void* xqt,
                      unsigned long long* counters, float* ratio_max, void* stream);
 
 /*
+ * apa_linear_wgrad for a block of output rows: dyqt and dw point at row r0 of
+ * dyq^T [N, M] and dw [N, K], and rows output rows are computed. The counts
+ * accumulate in counters across blocks; only the call with last != 0 folds
+ * counters[1]/counters[0] into *ratio_max and zeroes them, so a gradient made
+ * in row blocks yields the same values and the same ratio as one call. Lets a
+ * data-parallel backward start the all-reduce of finished rows while the next
+ * rows are computed. Same reference interfaces as apa_linear_wgrad.
+ */
+int apa_linear_wgrad_block(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt,
+                           float* dw, int64_t lddw, int64_t M, int64_t rows, int64_t K, int accumulate,
+                           unsigned long long* counters, float* ratio_max, int last, void* stream);
+
+/*
  * Scratch bytes apa_linear_wgrad_ws uses for this shape (same M, N, K as
  * apa_linear_wgrad), 0 when the weight gradient is not split.
  */

@@ -149,6 +149,93 @@ def test_buckets_follow_backward_order_two_ranks():
         assert marks[0] < total
 
 
+class _FakeApaLinear(nn.Module):
+    """The attributes GradientAverager and the row-block path use."""
+
+    def __init__(self, n, k):
+        super().__init__()
+        self.weight_master = nn.Parameter(torch.randn(n, k))
+        self.bias_master = nn.Parameter(torch.randn(n))
+        self._grad_ready_cb = None
+        self._dp = None
+
+
+class _ApaManager(_FakeManager):
+    def __init__(self, model, mods):
+        super().__init__(model)
+        self.apa_modules = mods
+
+
+def _blocks_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from apa.dp import GradientAverager
+        torch.manual_seed(0)
+        big, small = _FakeApaLinear(10, 6), _FakeApaLinear(4, 6)
+        model = nn.ModuleDict({"small": small, "big": big})
+        avg = GradientAverager(_ApaManager(model, {"small": small, "big": big}), None, bucket_bytes=1 << 20,
+                               block_bytes=200, block_rows=3)
+        out = {"blocked": [big._dp is avg and avg.buckets[avg.where[id(big.weight_master)]].blocks is not None,
+                           avg.buckets[avg.where[id(small.weight_master)]].blocks is None]}
+        W = big.weight_master
+        for step in range(2):
+            avg.arm()
+            local = {r: torch.randn(10, 6, generator=torch.Generator().manual_seed(10 * step + r)) for r in range(world)}
+            local_s = {r: torch.randn(4, 6, generator=torch.Generator().manual_seed(99 + 10 * step + r))
+                       for r in range(world)}
+            # the big layer's backward: its gradient in row blocks
+            blocks = avg.weight_blocks(big, W.grad)
+            out["blocks"] = blocks
+            for r0, r1 in blocks:
+                W.grad[r0:r1] = local[rank][r0:r1]
+                avg.weight_block_done(big, r0, r1)
+            out["again"] = avg.weight_blocks(big, W.grad)        # no second pass in one step
+            big.bias_master.grad.fill_(float(rank))
+            big._grad_ready_cb(big)
+            small.weight_master.grad.copy_(local_s[rank])
+            small.bias_master.grad.fill_(2.0 * rank)
+            small._grad_ready_cb(small)
+            nh = [len(b.handles) for b in avg.buckets]
+            avg.finish()
+            want = sum(local.values()) / world
+            want_s = sum(local_s.values()) / world
+            out[f"step{step}"] = (torch.equal(W.grad, want), torch.allclose(small.weight_master.grad, want_s),
+                                  big.bias_master.grad[0].item(), small.bias_master.grad[0].item(), nh)
+        out["unarmed"] = avg.weight_blocks(big, W.grad)
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_block_reduction_two_ranks():
+    """A large APALinear weight sits alone in its bucket and is reduced block
+    by block as its backward writes the rows; the bucket is not reduced again,
+    and every gradient ends up averaged exactly once."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_blocks_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in (0, 1):
+        o = out[r]
+        assert o["blocked"] == [True, True]
+        assert o["blocks"] == [(0, 3), (3, 6), (6, 9), (9, 10)]
+        assert o["again"] is None and o["unarmed"] is None
+        for step in (0, 1):
+            ok_w, ok_s, bb, sb, nh = o[f"step{step}"]
+            assert ok_w and ok_s
+            assert bb == 0.5 and sb == 1.0
+            # buckets in backward order: [big bias], [big weight: 4 blocks], [small bias + weight]
+            assert nh == [1, 4, 1]
+
+
 def _telemetry_worker(rank, world, port, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)

@@ -6,8 +6,10 @@ rank 1's batch carries an overflow spike. The reference evaluates local
 telemetry only (manager.py:221-256), so its ranks would disagree; here the
 telemetry is MAX-reduced before the ladder and the gradients are averaged, so
 every rank must skip that step, escalate the same layers, and keep
-bit-identical weights. NVLS is disabled so a rank that fails an assertion
-cannot leave a multicast binding behind."""
+bit-identical weights. With row blocks on, the first layer's weight gradient
+is computed and all-reduced in four row blocks; the replicas must then equal
+those of the whole-bucket reduction bit for bit. NVLS is disabled so a rank
+that fails an assertion cannot leave a multicast binding behind."""
 import os
 import socket
 
@@ -28,7 +30,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q, graphed):
+def _worker(rank, world, port, q, graphed, blocks):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -52,7 +54,7 @@ def _worker(rank, world, port, q, graphed):
         torch.manual_seed(0)
         model = nn.Sequential(APALinear(256, 256, config=cfg), nn.ReLU(), LayerNorm32(256),
                               APALinear(256, 16, config=cfg)).to(dev)
-        mgr = APAManager(model, cfg)
+        mgr = APAManager(model, cfg, dp_block_bytes=1 if blocks else 0, dp_block_rows=64)
         opt = torch.optim.AdamW(mgr.get_trainable_parameters(), lr=1e-3)
         g = torch.Generator().manual_seed(100 + rank)
         keeps, levels = [], []
@@ -84,25 +86,22 @@ def _worker(rank, world, port, q, graphed):
             levels.append([m.level for m in mgr.apa_modules.values()])
         torch.cuda.synchronize()
         gstep = None   # a graph holding NCCL work is released before the group
+        used = [len(b.blocks) for b in mgr._dp.buckets if b.blocks is not None and b.blocks_issued]
         weights = [p.detach().double().cpu() for p in mgr.get_trainable_parameters()]
-        q.put((rank, keeps, levels, [w.sum().item() for w in weights], [w.abs().sum().item() for w in weights]))
+        q.put((rank, keeps, levels, [w.sum().item() for w in weights], [w.abs().sum().item() for w in weights],
+               used))
     except Exception as e:   # report, then leave the group normally
-        q.put((rank, "error", repr(e), None, None))
+        q.put((rank, "error", repr(e), None, None, None))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("graphed", [False, True])
-def test_ranks_take_identical_decisions(graphed):
-    """graphed: the step replayed from a CUDA graph (reductions captured on a
-    forked stream, ladder gated on the step's compute)."""
+def _run(graphed, blocks, world=2):
     import torch.multiprocessing as mp
-    world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, graphed)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, graphed, blocks)) for r in range(world)]
     for p in procs:
         p.start()
     out = dict((r[0], r[1:]) for r in (q.get(timeout=300) for _ in procs))
@@ -111,12 +110,34 @@ def test_ranks_take_identical_decisions(graphed):
         assert p.exitcode == 0
     for r in range(world):
         assert out[r][0] != "error", out[r]
-    keeps0, levels0, sums0, abs0 = out[0]
+    keeps0, levels0, sums0, abs0, used0 = out[0]
     for r in range(1, world):
-        keeps, levels, sums, abss = out[r]
+        keeps, levels, sums, abss, used = out[r]
         assert keeps == keeps0
         assert levels == levels0
         assert sums == sums0 and abss == abs0     # bit-identical replicas
+        assert used == used0
     assert keeps0[SPIKE_STEP] is False            # only rank 1 saw the spike; every rank skips
     assert all(keeps0[s] for s in range(STEPS) if s != SPIKE_STEP)
     assert levels0[SPIKE_STEP][0] == 1            # the first layer escalated on every rank
+    return out[0]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("graphed", [False, True])
+def test_ranks_take_identical_decisions(graphed):
+    """graphed: the step replayed from a CUDA graph (reductions captured on a
+    forked stream, ladder gated on the step's compute)."""
+    assert _run(graphed, blocks=False)[4] == []
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("graphed", [False, True])
+def test_row_block_reduction_matches_whole(graphed):
+    """The first layer's 256x256 weight gradient in four 64-row blocks, each
+    all-reduced as soon as it is written: same decisions and bit-identical
+    weights as the whole-bucket reduction."""
+    whole = _run(graphed, blocks=False)
+    blocked = _run(graphed, blocks=True)
+    assert blocked[4] == [4]
+    assert blocked[:4] == whole[:4]

@@ -100,3 +100,42 @@ def test_large_outputs_are_not_split(L):
     with tiles: no split, no scratch."""
     for rung in (0, 1, 2):
         assert workspace_bytes(L, rung, 8192, 4096, 4096) == 0
+
+
+@pytest.mark.parametrize("rung", [0, 1, 2])
+def test_row_blocks_equal_whole(L, rung):
+    """apa_linear_wgrad_block over row blocks (ragged ones included) gives the
+    whole call's gradient bit for bit and, folded once at the last block, the
+    same underflow ratio; the counters are zero again afterwards."""
+    M, N, K = 4096, 1000, 384
+    rng = seeded("blocks", rung)
+    x = (rng.integers(-8, 9, size=(M, K)) / 32.0).astype(np.float32)
+    dy = (rng.integers(-8, 9, size=(M, N)) / 32.0).astype(np.float32)
+    dy[rng.random((M, N)) < 0.7] = 0.0
+    DYT, XT = padded(np.ascontiguousarray(dy.T), TDT[rung]), padded(np.ascontiguousarray(x.T), TDT[rung])
+    cnt = torch.zeros(3, dtype=torch.int64, device="cuda")
+    s = L.stream_handle()
+    whole = torch.empty(N, K, device="cuda")
+    r_whole = torch.zeros(1, device="cuda")
+    L.check(L.lib().apa_linear_wgrad(rung, DYT.data_ptr(), DYT.stride(0), XT.data_ptr(), XT.stride(0),
+                                     whole.data_ptr(), K, M, N, K, 0, cnt.data_ptr(), r_whole.data_ptr(), s),
+            "apa_linear_wgrad")
+    blocked = torch.full((N, K), 7.0, device="cuda")
+    r_blk = torch.zeros(1, device="cuda")
+    es = DYT.element_size()
+    blocks = [(0, 256), (256, 512), (512, 777), (777, 1000)]
+    for i, (r0, r1) in enumerate(blocks):
+        L.check(L.lib().apa_linear_wgrad_block(rung, DYT.data_ptr() + r0 * DYT.stride(0) * es, DYT.stride(0),
+                                               XT.data_ptr(), XT.stride(0), blocked.data_ptr() + r0 * K * 4, K, M,
+                                               r1 - r0, K, 0, cnt.data_ptr(), r_blk.data_ptr(),
+                                               int(i == len(blocks) - 1), s), "apa_linear_wgrad_block")
+        if i < len(blocks) - 1:
+            torch.cuda.synchronize()
+            assert r_blk.item() == 0.0                   # nothing folded before the last block
+    torch.cuda.synchronize()
+    assert torch.equal(blocked, whole)
+    assert r_blk.item() == r_whole.item()
+    if rung == 0:
+        assert r_whole.item() > 0.0                      # sums below 2^-6 underflow at the FP8 rung
+    assert cnt.cpu().tolist() == [0, 0, 0]
+    assert L.device_status() == 0
