@@ -459,28 +459,46 @@ __global__ void __launch_bounds__(256) underflow_kernel(const void* src, int64_t
 // Bias gradient: sum the per-64-row partials in a fixed order, round to the
 // working dtype (the autograd engine's cast to bias_work's dtype) and widen
 // to fp32 for bias_master.grad (manager.py:200-204).
-__global__ void __launch_bounds__(256) colsum_finalize_kernel(const float* partial, int64_t nparts, int64_t cols,
-                                                              int work_dt, float* out, int accumulate) {
-  // block: 32 columns x 8 warps; warp w sums partial rows w, w+8, ... in
-  // order, then warp 0 adds the 8 warp sums in order (deterministic)
-  __shared__ float part[8][32];
+constexpr int kColsumWarps = 32;
+__global__ void __launch_bounds__(kColsumWarps * 32) colsum_finalize_kernel(const float* partial, int64_t nparts,
+                                                                           int64_t cols, int work_dt, float* out,
+                                                                           int accumulate) {
+  // block: 32 columns x 32 warps; warp w sums partial rows w, w+32, ... in
+  // order (eight loads in flight), then warp 0 adds the 32 warp sums in order
+  // (deterministic)
+  __shared__ float part[kColsumWarps][33];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int64_t c = (int64_t)blockIdx.x * 32 + lane;
   float s = 0.0f;
-  if (c < cols)
-    for (int64_t r = w; r < nparts; r += 8) s += partial[r * cols + c];
+  if (c < cols) {
+    int64_t r = w;
+    for (; r + 7 * kColsumWarps < nparts; r += 8 * kColsumWarps) {
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = partial[(r + k * kColsumWarps) * cols + c];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s += v[k];
+    }
+    for (; r < nparts; r += kColsumWarps) s += partial[r * cols + c];
+  }
   part[w][lane] = s;
   __syncthreads();
   if (w == 0 && c < cols) {
     float t = 0.0f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) t += part[k][lane];
+    for (int k = 0; k < kColsumWarps; ++k) t += part[k][lane];
     float q;
     if (work_dt == APA_DT_E4M3) q = e4m3_to_f32(e4m3_from_f32(t));
     else if (work_dt == APA_DT_F16) q = f16_to_f32(f16_from_f32(t));
     else q = t;
     out[c] = accumulate ? out[c] + q : q;
   }
+}
+
+void launch_colsum_finalize(const float* partial, int64_t nparts, int64_t cols, int work_dt, float* out,
+                            int accumulate, cudaStream_t s) {
+  const unsigned grid = (unsigned)((cols + 31) / 32);
+  colsum_finalize_kernel<<<grid, kColsumWarps * 32, 0, s>>>(partial, nparts, cols, work_dt, out, accumulate);
 }
 
 // Zero a list of int32 words (per-step flag reset, manager.py:161-168).
@@ -608,9 +626,7 @@ extern "C" int apa_colsum_finalize(const float* partial, int64_t nparts, int64_t
                                    float* out, int accumulate, void* stream) {
   if (!partial || !out || nparts < 0 || cols < 0) return APA_ERR_INVALID;
   if (cols == 0) return APA_OK;
-  const unsigned grid = (unsigned)((cols + 31) / 32);
-  colsum_finalize_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(partial, nparts, cols, work_dtype,
-                                                                              out, accumulate);
+  launch_colsum_finalize(partial, nparts, cols, work_dtype, out, accumulate, static_cast<cudaStream_t>(stream));
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }
 

@@ -1073,37 +1073,74 @@ int launch_bn(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea
 // the GEMM: counts of nonzero / underflow values (on the fp32 sum; at FP16 on
 // its fp16 rounding), the rounding to the working dtype and the fp32 store
 // (or accumulate), and the last block's ratio fold into the running max.
-template <int KIND>
+template <int KIND, bool VEC>
 __global__ void __launch_bounds__(256) wgrad_reduce_kernel(const float* ws, int splits, int64_t slice, int64_t ld_ws,
                                                            int rows, int cols, float* dw, int64_t lddw, int accumulate,
                                                            float vmin, unsigned long long* counters,
                                                            float* ratio_max) {
+  // VEC: four adjacent columns per thread (cols, ld_ws and lddw multiples of
+  // 4, dw 16-byte aligned); rows * cols < 2^31 (the split path only takes
+  // small gradients)
+  constexpr int V = VEC ? 4 : 1;
   __shared__ unsigned int s_nz[8], s_uf[8];
   const uint32_t vb = __float_as_uint(vmin);
   unsigned int nz = 0, uf = 0;
-  const int64_t total = (int64_t)rows * cols;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
-    const int64_t r = e / cols, c = e - r * cols;
-    const float* src = ws + r * ld_ws + c;
-    float acc = src[0];
-    for (int sp = 1; sp < splits; ++sp) acc += src[sp * slice];
-    float out;
-    if constexpr (KIND == KIND_E4M3) {
-      const uint32_t a = (__float_as_uint(acc) & 0x7FFFFFFFu) - 1u;
-      nz += a < 0x7F800000u ? 1u : 0u;
-      uf += a < vb - 1u ? 1u : 0u;
-      out = e4m3_to_f32(e4m3_from_f32(acc));
-    } else if constexpr (KIND == KIND_F16) {
-      out = f16_to_f32(f16_from_f32(acc));
-      const uint32_t a = (__float_as_uint(out) & 0x7FFFFFFFu) - 1u;
-      nz += a < 0x7F800000u ? 1u : 0u;
-      uf += a < vb - 1u ? 1u : 0u;
+  const uint32_t cq = (uint32_t)(cols / V);
+  const uint32_t total = (uint32_t)rows * cq;
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t e = blockIdx.x * blockDim.x + threadIdx.x; e < total; e += stride) {
+    const uint32_t r = e / cq, c = (e - r * cq) * V;
+    const float* src = ws + (int64_t)r * ld_ws + c;
+    float acc[V];
+    if constexpr (VEC) {
+      const float4 v = *reinterpret_cast<const float4*>(src);
+      acc[0] = v.x; acc[1] = v.y; acc[2] = v.z; acc[3] = v.w;
     } else {
-      out = acc;
+      acc[0] = src[0];
     }
-    float* d = dw + r * lddw + c;
-    *d = accumulate ? *d + out : out;
+    // at most 8 splits: every split's load is issued before the adds, which
+    // run in split order
+#pragma unroll
+    for (int sp = 1; sp < 8; ++sp) {
+      if (sp < splits) {
+        if constexpr (VEC) {
+          const float4 v = *reinterpret_cast<const float4*>(src + sp * slice);
+          acc[0] += v.x; acc[1] += v.y; acc[2] += v.z; acc[3] += v.w;
+        } else {
+          acc[0] += src[sp * slice];
+        }
+      }
+    }
+    float res[V];
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      float out;
+      if constexpr (KIND == KIND_E4M3) {
+        const uint32_t a = (__float_as_uint(acc[i]) & 0x7FFFFFFFu) - 1u;
+        nz += a < 0x7F800000u ? 1u : 0u;
+        uf += a < vb - 1u ? 1u : 0u;
+        out = e4m3_to_f32(e4m3_from_f32(acc[i]));
+      } else if constexpr (KIND == KIND_F16) {
+        out = f16_to_f32(f16_from_f32(acc[i]));
+        const uint32_t a = (__float_as_uint(out) & 0x7FFFFFFFu) - 1u;
+        nz += a < 0x7F800000u ? 1u : 0u;
+        uf += a < vb - 1u ? 1u : 0u;
+      } else {
+        out = acc[i];
+      }
+      res[i] = out;
+    }
+    float* d = dw + (int64_t)r * lddw + c;
+    if constexpr (VEC) {
+      float4 o = make_float4(res[0], res[1], res[2], res[3]);
+      if (accumulate) {
+        const float4 old = *reinterpret_cast<const float4*>(d);
+        o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+      }
+      *reinterpret_cast<float4*>(d) = o;
+    } else {
+      *d = accumulate ? *d + res[0] : res[0];
+    }
   }
   if (!counters) return;
 #pragma unroll
@@ -1436,7 +1473,10 @@ extern "C" int apa_linear_wgrad_ws(int rung, const void* dyqt, int64_t lddyt, co
   if (rung != APA_RUNG_TF32 && !counters) return APA_ERR_INVALID;
   const apa::SplitPlan sp = apa::plan_wgrad_split(rung, N, K, M);
   const int64_t need = sp.splits > 1 ? (int64_t)sp.splits * sp.rows_pad * sp.ld_ws * 4 : 0;
-  if (need == 0 || !workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15u))
+  // the reduction kernel takes at most 8 splits and 32-bit element indices
+  // (the plan only splits outputs of a few tiles, so neither limit is reached)
+  if (need == 0 || !workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15u) ||
+      N * K >= (1ll << 31) || sp.splits > 8)
     return apa_linear_wgrad(rung, dyqt, lddyt, xqt, ldxt, dw, lddw, M, N, K, accumulate, counters, ratio_max,
                             stream);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1448,23 +1488,24 @@ extern "C" int apa_linear_wgrad_ws(int rung, const void* dyqt, int64_t lddyt, co
   if (int st = apa::gemm_dispatch(rung, apa::gemm::EPI_RAW, dyqt, lddyt, xqt, ldxt, ea, tile, 0, s)) return st;
   // phase 2: ordered sum + the weight-gradient epilogue
   const float vmin = rung == APA_RUNG_FP8 ? 0.015625f : rung == APA_RUNG_FP16 ? 6.1035e-5f : 0.0f;
-  const int64_t total = N * K;
+  const bool vec = (K % 4) == 0 && (lddw % 4) == 0 && (reinterpret_cast<uintptr_t>(dw) & 15u) == 0;
+  const int64_t total = vec ? N * K / 4 : N * K;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, (int64_t)apa::num_sms() * 4));
   const float* ws = static_cast<const float*>(workspace);
   const int64_t slice = sp.rows_pad * sp.ld_ws;
   using namespace apa::gemm;
+#define APA_WGRAD_REDUCE(KIND_)                                                                                  \
+  if (vec)                                                                                                       \
+    wgrad_reduce_kernel<KIND_, true><<<grid, 256, 0, s>>>(ws, sp.splits, slice, sp.ld_ws, (int)N, (int)K, dw,    \
+                                                          lddw, accumulate, vmin, counters, ratio_max);          \
+  else                                                                                                           \
+    wgrad_reduce_kernel<KIND_, false><<<grid, 256, 0, s>>>(ws, sp.splits, slice, sp.ld_ws, (int)N, (int)K, dw,   \
+                                                           lddw, accumulate, vmin, counters, ratio_max);
   switch (rung) {
-    case APA_RUNG_FP8:
-      wgrad_reduce_kernel<KIND_E4M3><<<grid, 256, 0, s>>>(ws, sp.splits, slice, sp.ld_ws, (int)N, (int)K, dw, lddw,
-                                                          accumulate, vmin, counters, ratio_max);
-      break;
-    case APA_RUNG_FP16:
-      wgrad_reduce_kernel<KIND_F16><<<grid, 256, 0, s>>>(ws, sp.splits, slice, sp.ld_ws, (int)N, (int)K, dw, lddw,
-                                                         accumulate, vmin, counters, ratio_max);
-      break;
-    default:
-      wgrad_reduce_kernel<KIND_TF32><<<grid, 256, 0, s>>>(ws, sp.splits, slice, sp.ld_ws, (int)N, (int)K, dw, lddw,
-                                                          accumulate, vmin, counters, ratio_max);
+    case APA_RUNG_FP8: APA_WGRAD_REDUCE(KIND_E4M3) break;
+    case APA_RUNG_FP16: APA_WGRAD_REDUCE(KIND_F16) break;
+    default: APA_WGRAD_REDUCE(KIND_TF32)
   }
+#undef APA_WGRAD_REDUCE
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }

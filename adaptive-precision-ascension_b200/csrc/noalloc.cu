@@ -83,7 +83,6 @@ extern "C" int apa_bias_grad_noalloc(const void* dy, int dy_dtype, int64_t rows,
   p.vec_dst = 0; p.vec_dst_t = 0;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (int st = cast_dispatch(dy_dtype, work_dtype, p, s)) return st;
-  const unsigned grid = (unsigned)((cols + 31) / 32);
-  colsum_finalize_kernel<<<grid, 256, 0, s>>>(scratch, nparts, cols, work_dtype, db, accumulate);
+  launch_colsum_finalize(scratch, nparts, cols, work_dtype, db, accumulate, s);
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }

@@ -266,6 +266,10 @@ def run_ours(args):
     del x, dy32, dy16
     torch.cuda.empty_cache()
     gpt = {}
+    vit = None
+    if args.vit:
+        vit = run_vit(torch, world, rank, dev, args.gpt_steps, max(4, args.warmup), barrier, max_over_ranks,
+                      graphed=not args.gpt_eager)
     for name in args.gpt:
         gpt[name] = run_gpt(torch, dist, name, world, rank, dev, args.gpt_steps, max(4, args.warmup), barrier,
                             max_over_ranks, graphed=not args.gpt_eager, optimizer=args.gpt_optimizer,
@@ -291,6 +295,7 @@ def run_ours(args):
             "optimizer": optim,
             "e2e": e2e,
             "gpt": gpt,
+            "vit": vit,
             "gpu_launches": launches,
             "clocks": clocks,
             "peaks": pk,
@@ -484,6 +489,130 @@ def run_gpt(torch, dist, name, world, rank, dev, steps, warmup, barrier, max_ove
            else "torch.optim.AdamW(fused=True)",
            "apa_linear_params": nparam, "levels": {["fp8", "fp16", "tf32"][k]: v for k, v in sorted(levels.items())},
            "loss": round(float(loss.item()), 4)}
+    del model, mgr, opt
+    torch.cuda.empty_cache()
+    return out
+
+
+# ViT classifier on 32x32x3 images: patch 4 (48-wide patch embedding, 64
+# patches + a class token = 65 tokens), d 512, depth 6, 8 heads, MLP 1024, 10
+# classes, APALinear for the patch embedding, QKV, projection, MLP and head;
+# per-GPU batch 512, pixels ~ N(0,1), uniform labels, conservative() config.
+VIT_CONFIG = dict(img=32, patch=4, ch=3, d=512, depth=6, heads=8, mlp=1024, classes=10, batch=512, lr=1e-3)
+
+
+def build_vit(torch, nn, F, apa, cfgd, device):
+    from apa import APAConfig, APALinear
+    cfg = APAConfig.conservative(device=str(device))
+    d, H, P = cfgd["d"], cfgd["heads"], cfgd["patch"]
+    n_patch = (cfgd["img"] // P) ** 2
+    pdim = cfgd["ch"] * P * P
+
+    class LayerNorm32(nn.LayerNorm):
+        def forward(self, x):
+            return F.layer_norm(x.float(), self.normalized_shape, self.weight, self.bias, self.eps)
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.norm1 = LayerNorm32(d)
+            self.qkv = APALinear(d, 3 * d, config=cfg)
+            self.out_proj = APALinear(d, d, config=cfg)
+            self.norm2 = LayerNorm32(d)
+            self.mlp = nn.Sequential(APALinear(d, cfgd["mlp"], config=cfg), nn.GELU(),
+                                     APALinear(cfgd["mlp"], d, config=cfg))
+
+        def forward(self, x):
+            B, T, C = x.shape
+            q, k, v = self.qkv(self.norm1(x)).to(torch.bfloat16).split(C, dim=2)
+            q, k, v = (t.view(B, T, H, C // H).transpose(1, 2) for t in (q, k, v))
+            a = F.scaled_dot_product_attention(q, k, v)
+            x = x + self.out_proj(a.transpose(1, 2).reshape(B, T, C)).float()
+            return x + self.mlp(self.norm2(x)).float()
+
+    class ViT(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.patch_embed = APALinear(pdim, d, config=cfg)
+            self.cls_token = nn.Parameter(torch.zeros(1, 1, d))
+            self.pos_embed = nn.Parameter(torch.randn(1, n_patch + 1, d) * 0.02)
+            self.blocks = nn.ModuleList([Block() for _ in range(cfgd["depth"])])
+            self.norm = LayerNorm32(d)
+            self.head = APALinear(d, cfgd["classes"], config=cfg)
+
+        def forward(self, img):
+            B = img.shape[0]
+            g = cfgd["img"] // P
+            patches = img.view(B, cfgd["ch"], g, P, g, P).permute(0, 2, 4, 1, 3, 5).reshape(B, g * g, pdim)
+            x = self.patch_embed(patches).float()
+            x = torch.cat([self.cls_token.expand(B, -1, -1), x], dim=1) + self.pos_embed
+            for blk in self.blocks:
+                x = blk(x)
+            return self.head(self.norm(x[:, 0]))
+
+    torch.manual_seed(0)
+    return ViT().to(device), cfg
+
+
+def run_vit(torch, world, rank, dev, steps, warmup, barrier, max_over_ranks, graphed=True):
+    import torch.nn as nn
+    import torch.nn.functional as F
+    import apa
+    from apa import APAManager
+    cfgd = VIT_CONFIG
+    model, cfg = build_vit(torch, nn, F, apa, cfgd, dev)
+    mgr = APAManager(model, cfg)
+    opt = torch.optim.AdamW(mgr.get_trainable_parameters(), lr=cfgd["lr"], weight_decay=0.01, fused=True)
+    g = torch.Generator().manual_seed(4321 + rank)
+    B = cfgd["batch"]
+    batches = [(torch.randn(B, cfgd["ch"], cfgd["img"], cfgd["img"], generator=g).to(dev),
+                torch.randint(0, cfgd["classes"], (B,), generator=g).to(dev)) for _ in range(4)]
+
+    def loss_fn(x, y):
+        return F.cross_entropy(model(x).float(), y)
+
+    if graphed:
+        from apa.graphs import GraphedTrainStep
+        gstep = GraphedTrainStep(mgr, loss_fn, batches[0], warmup=2)
+
+        def step(i):
+            loss, keep = gstep(*batches[i % len(batches)])
+            if keep:
+                opt.step()
+            return loss
+    else:
+        def step(i):
+            x, y = batches[i % len(batches)]
+            mgr.pre_step()
+            opt.zero_grad(set_to_none=True)
+            loss = loss_fn(x, y)
+            loss.backward()
+            if mgr.post_backward_sync_and_eval():
+                opt.step()
+            return loss
+
+    for i in range(warmup):
+        step(i)
+    barrier()
+    s = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(steps):
+        loss = step(warmup + i)
+    e1.record(s)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps)
+    images = world * B
+    levels = {}
+    for m in mgr.apa_modules.values():
+        levels[m.level] = levels.get(m.level, 0) + 1
+    out = {"images_per_s": round(images / ms * 1e3, 1), "ms_per_step": round(ms, 3), "global_batch_images": images,
+           "mode": "cuda-graph replay of pre_step+fwd+bwd" if graphed else "eager",
+           "optimizer": "torch.optim.AdamW(fused=True)",
+           "apa_linear_params": sum(m.weight_master.numel() for m in mgr.apa_modules.values()),
+           "levels": {["fp8", "fp16", "tf32"][k]: v for k, v in sorted(levels.items())},
+           "loss": round(float(loss.item()), 4)}
+    gstep = None
     del model, mgr, opt
     torch.cuda.empty_cache()
     return out
@@ -876,6 +1005,34 @@ def profile_case(case: str):
         step(4)
         torch.cuda.synchronize()
         torch.cuda.cudart().cudaProfilerStop()
+    elif case == "step-vit":
+        # one eager ViT training step between cudaProfilerStart/Stop, after warm-up steps
+        import torch.nn as nn
+        import torch.nn.functional as F
+        import apa
+        from apa import APAManager
+        cfgd = VIT_CONFIG
+        model, cfg = build_vit(torch, nn, F, apa, cfgd, dev)
+        mgr = APAManager(model, cfg)
+        opt = torch.optim.AdamW(mgr.get_trainable_parameters(), lr=cfgd["lr"], weight_decay=0.01, fused=True)
+        gi = torch.Generator().manual_seed(4321)
+        B = cfgd["batch"]
+        xb = torch.randn(B, cfgd["ch"], cfgd["img"], cfgd["img"], generator=gi).to(dev)
+        yb = torch.randint(0, cfgd["classes"], (B,), generator=gi).to(dev)
+
+        def step():
+            mgr.pre_step()
+            opt.zero_grad(set_to_none=True)
+            F.cross_entropy(model(xb).float(), yb).backward()
+            if mgr.post_backward_sync_and_eval():
+                opt.step()
+        for _ in range(4):
+            step()
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStart()
+        step()
+        torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
     elif case == "adamw-fp8":
         # AdamW on the 4096x4096 master fused with its FP8 working copies
         p = torch.randn(N, K, device=dev, generator=g) * 0.02
@@ -905,6 +1062,8 @@ def main():
     ap.add_argument("--gpt", default="gpt-char,gpt2m",
                     help="GPT training workloads also timed (tokens/s), comma-separated; '' for none")
     ap.add_argument("--gpt-steps", type=int, default=10)
+    ap.add_argument("--no-vit", dest="vit", action="store_false",
+                    help="skip the ViT classifier workload (images/s)")
     ap.add_argument("--gpt-eager", action="store_true", help="time the GPT workloads without CUDA-graph replay")
     ap.add_argument("--gpt-optimizer", choices=["torch", "apa"], default="torch",
                     help="optimizer of the GPT workloads: torch.optim.AdamW(fused) or apa.optim.APAAdamW")
@@ -917,7 +1076,7 @@ def main():
     ap.add_argument("--profile-case", default=None,
                     help="run a few launches of one kernel for an ncu capture (gemm-fp8|gemm-fp16|gemm-tf32|gemm-fp8-k1024|cast|"
                          "dyprep), "
-                         "or one profiled step (step-fp8|step-fp16|step-tf32|step-gpt2m|step-gpt-char)")
+                         "or one profiled step (step-fp8|step-fp16|step-tf32|step-gpt2m|step-gpt-char|step-vit)")
     args = ap.parse_args()
     if args.profile_case:
         profile_case(args.profile_case)

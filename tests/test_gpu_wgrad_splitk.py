@@ -19,8 +19,9 @@ pytestmark = pytest.mark.gpu
 
 WD = {0: "e4m3", 1: "f16", 2: "f32"}
 TDT = {0: torch.float8_e4m3fn, 1: torch.float16, 2: torch.float32}
-# (tokens M, out N, in K): the char-level GPT's projections and a ragged case
-SHAPES = [(16384, 1152, 384), (16384, 384, 1536), (8192, 200, 136), (4096, 64, 64)]
+# (tokens M, out N, in K): the char-level GPT's projections, ragged cases and
+# one whose gradient rows are not a multiple of 4 floats (scalar reduction)
+SHAPES = [(16384, 1152, 384), (16384, 384, 1536), (8192, 200, 136), (4096, 64, 64), (8192, 96, 50)]
 
 
 @pytest.fixture(scope="module")
