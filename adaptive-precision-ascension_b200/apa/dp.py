@@ -4,9 +4,12 @@ The reference has no gradient synchronisation at all (its only collective is
 the overflow flag, manager.py:186-187). Data parallel training here averages
 every trainable gradient across ranks once per step. Gradients are grouped
 into flat fp32 buckets (in reverse registration order, roughly the order the
-backward produces them); each parameter's ``.grad`` is a view into its
-bucket, so the weight-gradient kernels and autograd write straight into the
-buffers that NCCL reduces, with no packing copies. A bucket's all-reduce is
+backward produces them; 64 MiB each by default: on two GPUs the char-level
+GPT ran at 6.89 ms per step with them against 7.07 ms with 5.5 MiB buckets,
+because the GEMMs leave SMs to the collective from the first bucket on).
+Each parameter's ``.grad`` is a view into its bucket, so the weight-gradient
+kernels and autograd write straight into the buffers that NCCL reduces, with
+no packing copies. A bucket's all-reduce is
 issued (asynchronously, on the process group's stream) as soon as all of its
 gradients are written, and buckets are issued in a fixed order so every rank
 runs the same collectives in the same sequence.
@@ -88,6 +91,7 @@ class GradientAverager:
                 seen.add(id(p))
         params = list(reversed(params))
         device = params[0].device if params else torch.device("cpu")
+        self.bucket_bytes = bucket_bytes
         owner = {id(m.weight_master): m for m in mgr.apa_modules.values()}
         blocked = {}
         if block_bytes > 0:

@@ -192,7 +192,8 @@ def run_ours(args):
         torch.manual_seed(0)
         lin = APALinear(K, N, config=cfg)
         lin.level = level
-        mgr = APAManager(nn.Sequential(lin), cfg, dp_block_bytes=args.dp_block_bytes)
+        mgr = APAManager(nn.Sequential(lin), cfg, bucket_bytes=args.dp_bucket_bytes,
+                         dp_block_bytes=args.dp_block_bytes)
         return lin, mgr
 
     results = {}
@@ -269,11 +270,11 @@ def run_ours(args):
     vit = None
     if args.vit:
         vit = run_vit(torch, world, rank, dev, args.gpt_steps, max(4, args.warmup), barrier, max_over_ranks,
-                      graphed=not args.gpt_eager)
+                      graphed=not args.gpt_eager, dp_bucket_bytes=args.dp_bucket_bytes)
     for name in args.gpt:
         gpt[name] = run_gpt(torch, dist, name, world, rank, dev, args.gpt_steps, max(4, args.warmup), barrier,
                             max_over_ranks, graphed=not args.gpt_eager, optimizer=args.gpt_optimizer,
-                            dp_block_bytes=args.dp_block_bytes)
+                            dp_block_bytes=args.dp_block_bytes, dp_bucket_bytes=args.dp_bucket_bytes)
     out = None
     if rank == 0:
         fp8 = results["fp8"]
@@ -425,14 +426,14 @@ def gpt_batches(torch, cfgd, rank, device, n=4):
 
 
 def run_gpt(torch, dist, name, world, rank, dev, steps, warmup, barrier, max_over_ranks, graphed=True,
-            optimizer="torch", dp_block_bytes=0):
+            optimizer="torch", dp_block_bytes=0, dp_bucket_bytes=64 << 20):
     import torch.nn as nn
     import torch.nn.functional as F
     import apa
     from apa import APAManager
     cfgd = GPT_CONFIGS[name]
     model, cfg = build_gpt(torch, nn, F, apa, cfgd, dev)
-    mgr = APAManager(model, cfg, dp_block_bytes=dp_block_bytes)
+    mgr = APAManager(model, cfg, bucket_bytes=dp_bucket_bytes, dp_block_bytes=dp_block_bytes)
     if optimizer == "apa":
         # AdamW with each APALinear weight's next working copy written in the same pass
         from apa.optim import APAAdamW
@@ -554,14 +555,14 @@ def build_vit(torch, nn, F, apa, cfgd, device):
     return ViT().to(device), cfg
 
 
-def run_vit(torch, world, rank, dev, steps, warmup, barrier, max_over_ranks, graphed=True):
+def run_vit(torch, world, rank, dev, steps, warmup, barrier, max_over_ranks, graphed=True, dp_bucket_bytes=64 << 20):
     import torch.nn as nn
     import torch.nn.functional as F
     import apa
     from apa import APAManager
     cfgd = VIT_CONFIG
     model, cfg = build_vit(torch, nn, F, apa, cfgd, dev)
-    mgr = APAManager(model, cfg)
+    mgr = APAManager(model, cfg, bucket_bytes=dp_bucket_bytes)
     opt = torch.optim.AdamW(mgr.get_trainable_parameters(), lr=cfgd["lr"], weight_decay=0.01, fused=True)
     g = torch.Generator().manual_seed(4321 + rank)
     B = cfgd["batch"]
@@ -1067,6 +1068,8 @@ def main():
     ap.add_argument("--gpt-eager", action="store_true", help="time the GPT workloads without CUDA-graph replay")
     ap.add_argument("--gpt-optimizer", choices=["torch", "apa"], default="torch",
                     help="optimizer of the GPT workloads: torch.optim.AdamW(fused) or apa.optim.APAAdamW")
+    ap.add_argument("--dp-bucket-bytes", type=int, default=64 << 20,
+                    help="data parallel gradient bucket size in bytes")
     ap.add_argument("--dp-block-bytes", type=int, default=0,
                     help="data parallel: APALinear weights this large have their gradient computed and all-reduced "
                          "in row blocks (0, the default: one all-reduce per bucket after the whole gradient; "
