@@ -235,8 +235,9 @@ int apa_gemm_plan(int rung, int epilogue, int64_t M, int64_t N, int64_t K, int o
  * torch.optim.AdamW's order of operations (decoupled decay, bias-corrected
  * step `step` >= 1) and, in the same pass, the updated p cast to work_dtype
  * (E4M3, F16 or TF32) into wq and/or its transpose wq_t, with max |cast
- * value| written to *w_amax (which is reset first). APA_ERR_UNSUPPORTED for layouts the streaming
- * cast does not take (rows must be 16-byte aligned). Replaces the optimizer
+ * value| written to *w_amax (which is reset first). Every row pitch and base
+ * address must be 16-byte aligned (TMA tiles in and out); APA_ERR_UNSUPPORTED
+ * otherwise. Replaces the optimizer
  * step plus the weight half of the working-copy refresh in pre_step
  * (manager.py:145-172, layers.py:368-372).
  */
