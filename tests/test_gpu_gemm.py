@@ -1,7 +1,7 @@
 """K2-K4 tcgen05 GEMMs with their fused epilogues, through the C ABI.
 
 Tolerances (normwise relative error ||got - ref|| / ||ref||):
-  FP8 / FP16 rungs  2e-2   (BASELINE tolerance for GEMM outputs and gradients)
+  FP8 / FP16 rungs  2e-2   (the parity tolerance for GEMM outputs and gradients)
   TF32 rung         1e-3
 Telemetry (amax, NaN flag) is bit-exact against the kernel's own output, and
 the underflow counts are bit-exact against the oracle on inputs whose fp32
