@@ -172,10 +172,18 @@ def test_forward_telemetry_on_pair_tiles(L, rung):
     assert L.device_status() == 0
 
 
+def test_plan_long_reductions(L):
+    """Shapes whose CTAs run only one or two tiles but long reductions keep
+    the deeper four-warp pipeline; a long TF32 reduction takes the CTA pair."""
+    assert plan(L, 0, EPI_FWD, 8192, 1024, 4096, torch.float32) == (256, 4)
+    assert plan(L, 1, EPI_DGRAD, 8192, 1024, 4096, torch.bfloat16) == (256, 4)
+    assert plan(L, 2, EPI_DGRAD, 8192, 1024, 50304, torch.float32) == (512, 4)
+
+
 @pytest.mark.parametrize("rung", [0, 1, 2])
 def test_small_k_plan_uses_eight_epilogue_warps(L, rung):
-    """K = 1024 at FP8 (an epilogue-bound shape of a GPT-2-medium layer) and a
-    one-wave schedule both take 8 epilogue warps; the fused forward stays exact."""
+    """Epilogue-bound shapes (K = 1024 at FP8, a GPT-2-medium layer; K = 256 at
+    FP16 / TF32) take 8 epilogue warps; the fused forward stays exact."""
     M, K, N = 2048, 1024 if rung == 0 else 256, 1024
     ydt = torch.float16 if rung == 1 else torch.float32
     assert plan(L, rung, EPI_FWD, M, N, K, ydt)[1] == 8
