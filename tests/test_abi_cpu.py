@@ -50,3 +50,63 @@ def test_invalid_arguments_rejected_without_gpu():
                                None, None) == _lib.ERR_INVALID
     assert lib.apa_amax(None, 0, 5, None, None, None) == _lib.ERR_INVALID
     assert lib.apa_zero_list(None, 3, None) == _lib.ERR_INVALID
+
+
+def _params():
+    """name -> list of parameter type strings, from the header's declarations."""
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    out = {}
+    for name, params in re.findall(r"\b(?:int|unsigned|const char\s*\*|void)\s+\**\s*(apa_[a-z0-9_]+)\s*\(([^)]*)\)\s*;",
+                                   src, flags=re.S):
+        ps = [] if params.strip() in ("", "void") else [" ".join(p.split()) for p in params.split(",")]
+        out[name] = ps
+    return out
+
+
+def test_ctypes_argument_types_match_header():
+    """Every ctypes argtype has the width of the C parameter it binds: int ->
+    c_int, int64_t -> c_int64, float -> c_float, double -> c_double, any
+    pointer -> a pointer-sized type."""
+    from apa import _lib
+    decl = _params()
+    assert set(decl) == set(_lib.SIGNATURES)
+    for name, ps in decl.items():
+        sig = _lib.SIGNATURES[name]
+        assert len(sig) == len(ps), (name, len(sig), len(ps))
+        for i, (p, t) in enumerate(zip(ps, sig)):
+            if "*" in p:
+                want = ctypes.sizeof(ctypes.c_void_p)
+            elif p.startswith("int64_t"):
+                want = 8
+            elif p.startswith("double"):
+                want = 8
+                assert t is ctypes.c_double, (name, i, p)
+            elif p.startswith("float"):
+                want = 4
+                assert t is ctypes.c_float, (name, i, p)
+            elif p.startswith("int") or p.startswith("unsigned"):
+                want = 4
+            else:
+                raise AssertionError(f"unparsed parameter {p!r} of {name}")
+            assert ctypes.sizeof(t) == want, (name, i, p, t)
+
+
+def test_new_entry_points_validate_without_gpu():
+    """Block weight gradient, fused optimizer and forensic statistics reject
+    bad arguments before touching the device."""
+    from apa import _lib
+    if not os.path.exists(_lib.LIB_PATH):
+        pytest.skip("library not built")
+    lib = _lib.lib()
+    # zero rows / null operands
+    assert lib.apa_linear_wgrad_block(0, 16, 16, 16, 16, 16, 16, 16, 0, 16, 0, 16, None, 1, None) == _lib.ERR_INVALID
+    assert lib.apa_linear_wgrad_block(0, None, 16, 16, 16, 16, 16, 16, 16, 16, 0, 16, None, 1, None) == _lib.ERR_INVALID
+    # step 0, no output copy, ld < cols
+    assert lib.apa_adamw_cast(16, 16, 16, 16, 4, 4, 4, 1e-3, 0.9, 0.999, 1e-8, 0.0, 0, 16, 3, 16, None, 0, None,
+                              None) == _lib.ERR_INVALID
+    assert lib.apa_adamw_cast(16, 16, 16, 16, 4, 4, 4, 1e-3, 0.9, 0.999, 1e-8, 0.0, 1, None, 3, 16, None, 0, None,
+                              None) == _lib.ERR_INVALID
+    assert lib.apa_adamw_cast(16, 16, 16, 16, 4, 8, 4, 1e-3, 0.9, 0.999, 1e-8, 0.0, 1, 16, 3, 16, None, 0, None,
+                              None) == _lib.ERR_INVALID
+    assert lib.apa_tensor_stats(None, 0, 10, 16, None) == _lib.ERR_INVALID
