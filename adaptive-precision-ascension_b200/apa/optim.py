@@ -5,12 +5,13 @@ The reference trains with ``torch.optim.AdamW(manager.get_trainable_parameters()
 and then re-casts every master weight in ``pre_step`` (manager.py:145-172,
 layers.py:368-372): the optimizer reads and writes p, grad, m, v and the
 refresh reads p again to write the working copies. ``APAAdamW`` does both in
-one pass per weight (``apa_adamw_cast``): the updated master is cast to the
-layer's working dtype (and its transposed copy when the backward needs it)
-while it is still in registers, and the weight's telemetry comes along; the
-following ``pre_step`` then skips that layer's weight cast. Every other
-parameter (biases, LayerNorm, embeddings) and any weight the fused kernel
-cannot take goes through torch's own AdamW update. Semantics are those of
+one pass per weight (``apa_adamw_cast``: p, g, m, v arrive by TMA tiles, p, m and v are updated
+in place and stored back, and the updated master is cast to the layer's
+working dtype, with its transposed copy when the backward needs it, while it
+is still in registers); the weight's telemetry comes along and the following
+``pre_step`` skips that layer's weight cast. Every other parameter (biases,
+LayerNorm, embeddings) and any weight the fused kernel cannot take goes
+through torch's fused AdamW (its step counters then live on the device). Semantics are those of
 ``torch.optim.AdamW`` (decoupled weight decay, no amsgrad); results agree to
 fp32 rounding.
 
