@@ -65,3 +65,34 @@ def test_no_cpu_compute_path():
     lin = APALinear(16, 16, config=APAConfig(device="cpu"))
     with pytest.raises(APAKernelError):
         lin(torch.randn(2, 16))
+
+
+def test_apa_adamw_host_path_matches_torch_adamw():
+    """APAAdamW's bookkeeping without the fused kernel (CPU parameters: every
+    weight takes torch's update): same parameters and state as
+    torch.optim.AdamW over several steps, bit for bit, and no fused update
+    counted."""
+    from apa import APAConfig, APALinear, APAManager
+    from apa.optim import APAAdamW
+    cfg = APAConfig(device="cpu")
+    torch.manual_seed(0)
+    model = nn.Sequential(APALinear(12, 8, config=cfg), nn.LayerNorm(8), APALinear(8, 4, config=cfg))
+    mgr = APAManager(model, cfg)
+    params = mgr.get_trainable_parameters()
+    twins = [p.detach().clone().requires_grad_(True) for p in params]
+    opt = APAAdamW(mgr, lr=3e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    ref = torch.optim.AdamW(twins, lr=3e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    g = torch.Generator().manual_seed(1)
+    for _ in range(4):
+        for p, t in zip(params, twins):
+            grad = torch.randn(p.shape, generator=g)
+            p.grad = grad.clone()
+            t.grad = grad.clone()
+        opt.step()
+        ref.step()
+    for p, t in zip(params, twins):
+        assert torch.equal(p.detach(), t.detach())
+        assert torch.equal(opt.state[p]["exp_avg"], ref.state[t]["exp_avg"])
+        assert torch.equal(opt.state[p]["exp_avg_sq"], ref.state[t]["exp_avg_sq"])
+        assert float(opt.state[p]["step"]) == float(ref.state[t]["step"]) == 4.0
+    assert opt.fused_steps == 0
