@@ -204,6 +204,13 @@ def _blocks_worker(rank, world, port, q):
             out[f"step{step}"] = (torch.equal(W.grad, want), torch.allclose(small.weight_master.grad, want_s),
                                   big.bias_master.grad[0].item(), small.bias_master.grad[0].item(), nh)
         out["unarmed"] = avg.weight_blocks(big, W.grad)
+        # the bucket view a backward writes into when the gradient was cleared
+        out["view_unarmed"] = avg.grad_view(W) is None
+        avg.arm()
+        v = avg.grad_view(W)
+        out["view_armed"] = v is not None and v.data_ptr() == W.grad.data_ptr() and v.shape == W.shape
+        out["view_foreign"] = avg.grad_view(torch.nn.Parameter(torch.zeros(3))) is None
+        avg.finish()
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
@@ -228,6 +235,7 @@ def test_row_block_reduction_two_ranks():
         assert o["blocked"] == [True, True]
         assert o["blocks"] == [(0, 3), (3, 6), (6, 9), (9, 10)]
         assert o["again"] is None and o["unarmed"] is None
+        assert o["view_unarmed"] and o["view_armed"] and o["view_foreign"]
         for step in (0, 1):
             ok_w, ok_s, bb, sb, nh = o[f"step{step}"]
             assert ok_w and ok_s
