@@ -131,6 +131,15 @@ def test_ranks_take_identical_decisions(graphed):
     assert _run(graphed, blocks=False)[4] == []
 
 
+@pytest.mark.parametrize("world", [4, 8])
+def test_ranks_take_identical_decisions_wider(world):
+    """The same check with 4 and 8 ranks (only rank 1 sees the spike), where
+    the box has that many GPUs."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    assert _run(False, blocks=False, world=world)[4] == []
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("graphed", [False, True])
 def test_row_block_reduction_matches_whole(graphed):
