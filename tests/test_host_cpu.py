@@ -96,3 +96,29 @@ def test_apa_adamw_host_path_matches_torch_adamw():
         assert torch.equal(opt.state[p]["exp_avg_sq"], ref.state[t]["exp_avg_sq"])
         assert float(opt.state[p]["step"]) == float(ref.state[t]["step"]) == 4.0
     assert opt.fused_steps == 0
+
+
+def test_event_log_lines_match_reference_records(tmp_path):
+    """The event logger writes the reference's JSONL records (telemetry.py:41-75):
+    the same keys in the same order and the same values as the events the
+    reference logged on the cfg0 trajectory, plus a timestamp."""
+    import json
+    import os
+    from apa.telemetry import APAEventLogger
+    golden = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "cfg0_trajectory.json")))
+    log = tmp_path / "events.jsonl"
+    lg = APAEventLogger(str(log))
+    for e in golden["events"]:
+        if e["event"] == "escalation":
+            lg.log_escalation(e["step"], e["module"], e["reason"], e["old_level"], e["new_level"], e["trigger_value"])
+        else:
+            lg.log_skip_batch(e["step"], e["reason"], e["trigger_modules"])
+    got = [json.loads(line) for line in open(log)]
+    assert len(got) == len(golden["events"])
+    for g, e in zip(got, golden["events"]):
+        assert list(g)[:-1] == list(e) and list(g)[-1] == "timestamp"
+        for k, v in e.items():
+            if isinstance(v, float) and math.isnan(v):
+                assert math.isnan(g[k])
+            else:
+                assert g[k] == v, k
