@@ -18,6 +18,13 @@ whole-job FLOP rate with time taken as the max over ranks.
 `--impl reference` times the reference's own implementation of the path (its
 fp8_simulation_mode CPU path, installed under baseline/_ref) on this host's
 cores, FP8 rung, on a bounded number of steps.
+
+Besides the headline, the JSON line carries: `rungs` (all three rungs),
+`roofline` (the FP8 forward GEMM timed alone, with the fused-telemetry cost),
+`optimizer` (the fused AdamW + working-copy kernel on the 4096x4096 master
+against torch's fused AdamW plus the cast), `e2e` (host-resident inputs copied
+every step), `gpt` (char nanoGPT and GPT-2-medium tokens/s) and `vit` (the ViT
+classifier's images/s), all at the same N; `cpu_baseline` at N=1.
 """
 from __future__ import annotations
 
