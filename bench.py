@@ -15,16 +15,20 @@ same layer on its own 8192-token shard (weak scaling) and the step includes the
 data-parallel gradient all-reduce and the telemetry all-reduce; `value` is the
 whole-job FLOP rate with time taken as the max over ranks.
 
-`--impl reference` times the reference's own implementation of the path (its
-fp8_simulation_mode CPU path, installed under baseline/_ref) on this host's
-cores, FP8 rung, on a bounded number of steps.
+`--impl reference` times the reference's own implementation of the path, its
+fp8_simulation_mode CPU path, on this host's cores, FP8 rung, on a bounded
+number of full steps, plus the cfg0 quick-start MLP's 200 steps: the reference
+package when it is installed under baseline/_ref, else the torch-CPU port of
+that path (oracle/ref_port.py, bit-exact against the reference's own outputs);
+`cpu_baseline.kind` says which ran.
 
 Besides the headline, the JSON line carries: `rungs` (all three rungs),
 `roofline` (the FP8 forward GEMM timed alone, with the fused-telemetry cost),
 `optimizer` (the fused AdamW + working-copy kernel on the 4096x4096 master
 against torch's fused AdamW plus the cast), `e2e` (host-resident inputs copied
 every step), `gpt` (char nanoGPT and GPT-2-medium tokens/s) and `vit` (the ViT
-classifier's images/s), all at the same N; `cpu_baseline` at N=1.
+classifier's images/s), all at the same N; `cpu_baseline` and `cfg0` (the
+quick-start MLP's steps/s through this library) at N=1.
 """
 from __future__ import annotations
 
@@ -308,6 +312,8 @@ def run_ours(args):
             "clocks": clocks,
             "peaks": pk,
         }
+        if world == 1:
+            out["cfg0"] = cfg0_gpu(torch, dev)
         if world == 1 and not args.no_cpu_baseline:
             out["cpu_baseline"] = cpu_baseline(args, sample_steps=1)
     if world > 1:
@@ -813,31 +819,49 @@ def run_e2e(torch, make, x, dy32, dev, args, world, barrier, max_over_ranks):
 # ---------------------------------------------------------------------------
 # the reference's CPU path
 # ---------------------------------------------------------------------------
-def _import_reference():
+def reference_impl():
+    """The reference's CPU implementation of the path, as (kind, module):
+    the reference package itself when it is installed under baseline/_ref
+    ("reference"), else the torch-CPU port of its fp8_simulation_mode path
+    (oracle/ref_port.py, "port"), which reproduces the reference's outputs,
+    telemetry and cfg0 trajectory bit for bit (tests/test_ref_port_cpu.py)
+    with the same torch operations, so it costs what the reference costs."""
     ref = os.path.join(ROOT, "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref, "apa")):
-        return None, "reference not installed under baseline/_ref"
-    for k in [k for k in sys.modules if k == "apa" or k.startswith("apa.")]:
-        del sys.modules[k]
-    sys.path.insert(0, ref)
-    try:
-        import apa as ref_apa
-    finally:
-        sys.path.remove(ref)
-    if not os.path.abspath(ref_apa.__file__).startswith(os.path.abspath(ref)):
-        return None, "could not import the reference package"
-    return ref_apa, None
+    if os.path.isdir(os.path.join(ref, "apa")):
+        for k in [k for k in sys.modules if k == "apa" or k.startswith("apa.")]:
+            del sys.modules[k]
+        sys.path.insert(0, ref)
+        try:
+            import apa as ref_apa
+        finally:
+            sys.path.remove(ref)
+        if os.path.abspath(ref_apa.__file__).startswith(os.path.abspath(ref)):
+            return "reference", ref_apa
+    if ROOT not in sys.path:
+        sys.path.insert(0, ROOT)
+    from oracle import ref_port
+    return "port", ref_port
 
 
-def ref_step_fn(ref_apa, torch, M_=M):
+def ref_step_fn(kind, mod, torch, level=0):
+    """One cfg1 training step (pre_step, forward, backward, evaluation) of the
+    reference's CPU path at the full 8192x4096x4096 shape, same seeds as the
+    GPU arm: layer initialised under torch.manual_seed(0), x bf16 N(0,1) from
+    a CPU generator seeded 0, dy N(0,1) seeded 1 (fp16 at the FP16 rung)."""
     import torch.nn as nn
-    cfg = ref_apa.APAConfig(fp8_simulation_mode=True, device="cpu", check_interval=1)
     torch.manual_seed(0)
-    lin = ref_apa.APALinear(K, N, config=cfg)
-    mgr = ref_apa.APAManager(nn.Sequential(lin), cfg)
-    g = torch.Generator().manual_seed(0)
-    x = torch.randn(M_, K, generator=g).to(torch.bfloat16).requires_grad_(True)
-    dy = torch.randn(M_, N, generator=torch.Generator().manual_seed(1))
+    if kind == "reference":
+        cfg = mod.APAConfig(fp8_simulation_mode=True, device="cpu", check_interval=1)
+        lin = mod.APALinear(K, N, config=cfg)
+        mgr = mod.APAManager(nn.Sequential(lin), cfg)
+    else:
+        lin = mod.PortLinear(K, N)
+        mgr = mod.PortManager(nn.Sequential(lin), check_interval=1)
+    lin.level = level
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16).requires_grad_(True)
+    dy = torch.randn(M, N, generator=torch.Generator().manual_seed(1))
+    if level == 1:
+        dy = dy.half()
 
     def step():
         mgr.pre_step()
@@ -847,64 +871,182 @@ def ref_step_fn(ref_apa, torch, M_=M):
     return step
 
 
-def cpu_baseline(args, sample_steps=1):
-    import torch
-    ref_apa, why = _import_reference()
-    if ref_apa is None:
-        return {"value": None, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "reference",
-                "sample": why}
-    torch.set_num_threads(os.cpu_count())
+CFG0_STEPS = 200
+CFG0_SPIKES = (50, 150)
+
+
+def cfg0_inputs(torch):
+    """cfg0's seeded batch: x [64, 768] N(0,1) and labels in [0, 10) from a
+    CPU generator seeded 0, then for each spike step (50 and 150, 0-based)
+    49 element indices (0.1 %) whose values are scaled by 1e3 on that step."""
+    g = torch.Generator().manual_seed(0)
+    x0 = torch.randn(64, 768, generator=g)
+    y0 = torch.randint(0, 10, (64,), generator=g)
+    spikes = {s: torch.randperm(x0.numel(), generator=g)[:49] for s in CFG0_SPIKES}
+    return x0, y0, spikes
+
+
+def cfg0_cpu(kind, mod, torch):
+    """cfg0 (APALinear(768,768) -> ReLU -> LayerNorm(768) -> APALinear(768,10),
+    AdamW 1e-3, research_default, batch 64, 200 steps with two input spikes)
+    on the reference's CPU path: steps/s over the 200 steps."""
+    import torch.nn as nn
+    import torch.nn.functional as F
+    torch.manual_seed(0)
+    if kind == "reference":
+        cfg = mod.APAConfig.research_default(fp8_simulation_mode=True, device="cpu")
+        lin = lambda i, o: mod.APALinear(i, o, config=cfg)
+    else:
+        lin = mod.PortLinear
+    model = nn.Sequential(lin(768, 768), nn.ReLU(), nn.LayerNorm(768), lin(768, 10))
+    if kind == "reference":
+        mgr = mod.APAManager(model, cfg)
+        params = mgr.get_trainable_parameters()
+    else:
+        mgr = mod.PortManager(model, theta=0.40, alpha=0.95, check_interval=4)
+        params = mgr.trainable()
+    opt = torch.optim.AdamW(params, lr=1e-3)
+    x0, y0, spikes = cfg0_inputs(torch)
+    skips = []
+    t0 = time.perf_counter()
+    for step in range(CFG0_STEPS):
+        x = x0.clone()
+        if step in spikes:
+            x.view(-1)[spikes[step]] *= 1e3
+        mgr.pre_step()
+        opt.zero_grad(set_to_none=True)
+        F.cross_entropy(model(x), y0).backward()
+        if mgr.post_backward_sync_and_eval():
+            opt.step()
+        else:
+            opt.zero_grad(set_to_none=True)
+            skips.append(step)
+    dt = time.perf_counter() - t0
+    return {"steps_per_s": round(CFG0_STEPS / dt, 2), "steps": CFG0_STEPS, "skipped_steps": skips,
+            "cores": torch.get_num_threads(), "kind": kind}
+
+
+def cfg0_gpu(torch, dev):
+    """cfg0 through this library's API on the GPU (same model, seeds, spikes
+    and optimizer as cfg0_cpu): steps/s over the 200 steps, each step ending
+    in the ladder's host read, timed with CUDA events on the current stream."""
+    import torch.nn as nn
+    import torch.nn.functional as F
+    from apa import APAConfig, APALinear, APAManager
+    cfg = APAConfig.research_default(device=str(dev))
+
+    class MixedLayerNorm(nn.LayerNorm):
+        # accepts the fp16 output of an FP16-rung layer (torch's CPU LayerNorm
+        # does, its CUDA one does not) and returns the input's dtype
+        def forward(self, x):
+            return F.layer_norm(x.float(), self.normalized_shape, self.weight, self.bias, self.eps).to(x.dtype)
+
+    torch.manual_seed(0)
+    model = nn.Sequential(APALinear(768, 768, config=cfg), nn.ReLU(), MixedLayerNorm(768),
+                          APALinear(768, 10, config=cfg)).to(dev)
+    mgr = APAManager(model, cfg)
+    opt = torch.optim.AdamW(mgr.get_trainable_parameters(), lr=1e-3)
+    x0, y0, spikes = cfg0_inputs(torch)
+    x0, y0 = x0.to(dev), y0.to(dev)
+    spikes = {k: v.to(dev) for k, v in spikes.items()}
+    skips = []
+    s = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for step in range(CFG0_STEPS):
+        x = x0.clone()
+        if step in spikes:
+            x.view(-1)[spikes[step]] *= 1e3
+        mgr.pre_step()
+        opt.zero_grad(set_to_none=True)
+        F.cross_entropy(model(x), y0).backward()
+        if mgr.post_backward_sync_and_eval():
+            opt.step()
+        else:
+            opt.zero_grad(set_to_none=True)
+            skips.append(step)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    return {"steps_per_s": round(CFG0_STEPS / ms * 1e3, 2), "steps": CFG0_STEPS, "skipped_steps": skips,
+            "mode": "eager, one host read per step"}
+
+
+def _quiet(fn, *a):
     import contextlib
     import io
-    step = ref_step_fn(ref_apa, torch)
-    with contextlib.redirect_stdout(io.StringIO()):
+    with contextlib.redirect_stdout(io.StringIO()):   # the reference's event logger prints
+        return fn(*a)
+
+
+def cpu_baseline(args, sample_steps=1):
+    import torch
+    kind, mod = reference_impl()
+    torch.set_num_threads(os.cpu_count())
+    step = ref_step_fn(kind, mod, torch)
+
+    def run():
         step()
         t0 = time.perf_counter()
         for _ in range(sample_steps):
             step()
-        dt = (time.perf_counter() - t0) / sample_steps
+        return (time.perf_counter() - t0) / sample_steps
+    dt = _quiet(run)
+    src = ("the reference's fp8_simulation_mode CPU path" if kind == "reference" else
+           "the torch-CPU port of the reference's fp8_simulation_mode path (oracle/ref_port.py)")
     return {"value": round(FLOPS_STEP / dt / 1e12, 4), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
-            "kind": "reference",
-            "sample": f"reference fp8_simulation_mode CPU path, FP8 rung, full 8192x4096x4096 step, "
-                      f"{sample_steps} timed step(s) after 1 warm-up, {dt:.2f} s/step, torch {torch.__version__}"}
+            "kind": kind,
+            "sample": f"{src}, FP8 rung, full 8192x4096x4096 step, {sample_steps} timed step(s) after 1 warm-up, "
+                      f"{dt:.2f} s/step, torch {torch.__version__}"}
 
 
 def run_reference(args):
+    """The reference arm: the reference's CPU implementation of the path on
+    this host's cores (all of them), FP8 rung at the full cfg1 shape, each
+    step a full training step; at most 10 timed steps after at most 2 warm-up
+    steps so the run stays within about a minute. Rank 0 only under torchrun."""
     world, rank, _ = dist_info()
     if rank != 0:
         return None
-    import contextlib
-    import io
     import torch
-    ref_apa, why = _import_reference()
-    if ref_apa is None:
-        return {"impl": "reference", "unavailable": why}
+    kind, mod = reference_impl()
     torch.set_num_threads(os.cpu_count())
-    step = ref_step_fn(ref_apa, torch)
-    steps = max(1, min(args.steps, 5))
-    warm = max(1, min(args.warmup, 1))
-    with contextlib.redirect_stdout(io.StringIO()):
+    step = ref_step_fn(kind, mod, torch)
+    steps = max(1, min(args.steps, 10))
+    warm = max(1, min(args.warmup, 2))
+
+    def run():
         for _ in range(warm):
             step()
         t0 = time.perf_counter()
         for _ in range(steps):
             step()
-        dt = (time.perf_counter() - t0) / steps
+        return (time.perf_counter() - t0) / steps
+    dt = _quiet(run)
+    cfg0 = _quiet(cfg0_cpu, kind, mod, torch)
     v = round(FLOPS_STEP / dt / 1e12, 4)
+    src = ("the reference's fp8_simulation_mode CPU path (baseline/_ref)" if kind == "reference" else
+           "the torch-CPU port of the reference's fp8_simulation_mode path (oracle/ref_port.py; the reference "
+           "package is not installed here)")
     return {"impl": "reference", "metric": METRIC, "value": v, "unit": "TFLOP/s", "n_gpus": world,
             "steps": steps, "warmup": warm, "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "e4m3", "data": "synthetic",
             "config": dict(CONFIG, parallelism="cpu"),
-            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": "reference",
-                             "sample": f"reference fp8_simulation_mode CPU path, FP8 rung, {steps} full steps "
-                                       f"(of the requested {args.steps}) after {warm} warm-up"},
-            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": torch.get_num_threads(), "kind": kind,
+                             "sample": f"{src}, FP8 rung, {steps} full 8192x4096x4096 steps (of the requested "
+                                       f"{args.steps}) after {warm} warm-up, torch {torch.__version__}"},
+            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "cfg0": cfg0}
 
 
 def profile_case(case: str):
     """A few launches of one kernel at the bench shape, for ncu captures:
-    gemm-fp8 / gemm-fp16 / gemm-tf32 (forward GEMM), cast (bf16 x -> E4M3 and
-    its transposed copy), dyprep (fp32 dy -> E4M3 + transposed + bias partials)."""
+    gemm-fp8 / gemm-fp16 / gemm-tf32 (forward GEMM), dgrad-<rung> and
+    wgrad-<rung> (input / weight gradient GEMMs), cast (bf16 x -> E4M3 and its
+    transposed copy), dyprep (fp32 dy -> E4M3 + transposed + bias partials),
+    cast-tf32 / dyprep-tf32 (the same at the TF32 rung), adamw-fp8, and
+    one-step launch lists (step-*)."""
     sys.path.insert(0, PKG)
     import torch
     from apa import _lib
@@ -935,6 +1077,45 @@ def profile_case(case: str):
         for _ in range(3):
             _lib.check(lib.apa_linear_fwd(rung, x.data_ptr(), K, w.data_ptr(), K, None, y.data_ptr(), N, M, N, K,
                                           amax.data_ptr(), flag.data_ptr(), st), "fwd")
+    elif case.split("-")[0] in ("dgrad", "wgrad"):
+        # input / weight gradient GEMM at the bench shape with its fused
+        # epilogue: dx bf16 with boundary-cast telemetry, or dw fp32 with the
+        # underflow counts and ratio fold
+        op, rname = case.split("-")
+        rung = {"fp8": 0, "fp16": 1, "tf32": 2}[rname]
+        dt = {0: torch.float8_e4m3fn, 1: torch.float16, 2: torch.float32}[rung]
+        dyq = torch.randn(M, N, device=dev, generator=g).to(dt)
+        amax = torch.zeros(1, device=dev)
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        if op == "dgrad":
+            wqt = (torch.randn(K, N, device=dev, generator=g) * 0.02).to(dt)
+            dx = torch.empty(M, K, dtype=torch.bfloat16, device=dev)
+            for _ in range(3):
+                _lib.check(lib.apa_linear_dgrad(rung, dyq.data_ptr(), N, wqt.data_ptr(), N, dx.data_ptr(),
+                                                _lib.DT_BF16, K, M, N, K, amax.data_ptr(), flag.data_ptr(), st),
+                           "dgrad")
+        else:
+            dyqt = dyq.t().contiguous()
+            xqt = torch.randn(K, M, device=dev, generator=g).to(dt)
+            dw = torch.empty(N, K, device=dev)
+            cnt = torch.zeros(3, dtype=torch.int64, device=dev)
+            for _ in range(3):
+                _lib.check(lib.apa_linear_wgrad(rung, dyqt.data_ptr(), M, xqt.data_ptr(), M, dw.data_ptr(), K, M, N,
+                                                K, 0, cnt.data_ptr(), amax.data_ptr(), st), "wgrad")
+    elif case in ("cast-tf32", "dyprep-tf32"):
+        # the TF32 rung's casts: x bf16 -> TF32-rounded fp32 and its transposed
+        # copy; dy fp32 -> TF32 + transposed + bias partial sums
+        src_dt, code = (torch.bfloat16, _lib.DT_BF16) if case == "cast-tf32" else (torch.float32, _lib.DT_F32)
+        src = torch.randn(M, K, device=dev, generator=g).to(src_dt)
+        q = torch.empty(M, K, device=dev)
+        qt = torch.empty(K, M, device=dev)
+        part = torch.empty(M // 64, K, device=dev) if case == "dyprep-tf32" else None
+        amax = torch.zeros(1, device=dev)
+        flag = torch.zeros(1, dtype=torch.int32, device=dev)
+        for _ in range(3):
+            _lib.check(lib.apa_cast(src.data_ptr(), code, M, K, K, q.data_ptr(), _lib.DT_TF32, K, qt.data_ptr(), M,
+                                    amax.data_ptr(), flag.data_ptr(), 1 if part is not None else 0, None,
+                                    _lib.ptr(part), st), case)
     elif case == "cast":
         x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
         xq = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=dev)
@@ -1084,8 +1265,9 @@ def main():
     ap.add_argument("--eager", action="store_true",
                     help="time the APALinear steps without CUDA-graph replay (every launch from the host)")
     ap.add_argument("--profile-case", default=None,
-                    help="run a few launches of one kernel for an ncu capture (gemm-fp8|gemm-fp16|gemm-tf32|gemm-fp8-k1024|cast|"
-                         "dyprep), "
+                    help="run a few launches of one kernel for an ncu capture (gemm-fp8|gemm-fp16|gemm-tf32|gemm-fp8-k1024|"
+                         "dgrad-fp8|dgrad-fp16|dgrad-tf32|wgrad-fp8|wgrad-fp16|wgrad-tf32|cast|dyprep|cast-tf32|"
+                         "dyprep-tf32|adamw-fp8), "
                          "or one profiled step (step-fp8|step-fp16|step-tf32|step-gpt2m|step-gpt-char|step-vit)")
     args = ap.parse_args()
     if args.profile_case:

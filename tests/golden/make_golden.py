@@ -2,7 +2,11 @@
 
 Run in a container that has the reference checkout (read-only) and torch:
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference [fixture ...]
+
+(or set APA_REFERENCE_DIR instead of the first argument). With fixture names
+(casts, underflow, linear_small, ladder, cfg0_trajectory, cfg1_variants) only
+those are regenerated.
 
 It imports the reference's ``apa`` package from that checkout, drives it on
 CPU with ``fp8_simulation_mode=True`` (the reference's CPU path) and writes:
@@ -16,6 +20,10 @@ CPU with ``fp8_simulation_mode=True`` (the reference's CPU path) and writes:
 * ``ladder.json``     APAManager evaluations on injected buffer values.
 * ``cfg0_trajectory.json`` the quick-start MLP run (200 steps, two input
                       spikes): escalation events, skipped steps, final levels.
+* ``cfg1_variants.json`` the single 8192x4096x4096 APALinear (check_interval
+                      1): the outlier variant's first step and the underflow
+                      variant run until its SILENT_UNDERFLOW escalation: per
+                      step underflow ratio, events and skipped steps.
 
 The fixtures are small; the GPU box never runs this script.
 """
@@ -32,7 +40,10 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+_ARGS = [a for a in sys.argv[1:]]
+REF = os.environ.get("APA_REFERENCE_DIR") or (_ARGS.pop(0) if _ARGS else None)
+if not REF or not os.path.isdir(os.path.join(REF, "apa")):
+    sys.exit("usage: make_golden.py /path/to/reference [fixture ...]  (or set APA_REFERENCE_DIR)")
 sys.path.insert(0, REF)
 
 import apa  # noqa: E402  (the reference package)
@@ -285,10 +296,63 @@ def cfg0_trajectory():
         json.dump(res, fh, allow_nan=True)
 
 
+def _cfg1_layer():
+    """The cfg1 layer as the bench builds it: APALinear(4096, 4096) initialised
+    under torch.manual_seed(0), default config with check_interval 1."""
+    torch.manual_seed(0)
+    cfg = APAConfig(fp8_simulation_mode=True, device="cpu", check_interval=1)
+    lin = APALinear(4096, 4096, config=cfg)
+    return lin, APAManager(nn.Sequential(lin), cfg)
+
+
+def cfg1_inputs(variant):
+    """cfg1 variant inputs from CPU generators: x [8192, 4096] N(0,1) (seed 0)
+    and dy N(0,1) (seed 1), in bf16 / fp32.
+    outlier: 0.05 % of x (a randperm of the same generator) scaled by 500;
+    underflow: a rand() < 0.5 mask of the same generator selects elements of
+    x scaled by 1e-4, and dy is scaled by 5e-4."""
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(8192, 4096, generator=g)
+    if variant == "outlier":
+        n = int(x.numel() * 0.0005)
+        idx = torch.randperm(x.numel(), generator=g)[:n]
+        x.view(-1)[idx] *= 500
+        dscale = 1.0
+    else:
+        mask = torch.rand(8192, 4096, generator=g) < 0.5
+        x = torch.where(mask, x * 1e-4, x)
+        dscale = 5e-4
+    dy = torch.randn(8192, 4096, generator=torch.Generator().manual_seed(1)) * dscale
+    return x.to(torch.bfloat16), dy
+
+
+def cfg1_variants(max_steps=80):
+    events = _capture_events()
+    out = {}
+    for variant in ("outlier", "underflow"):
+        lin, mgr = _cfg1_layer()
+        x, dy = cfg1_inputs(variant)
+        x.requires_grad_(True)
+        events.clear()
+        ratios, skips, nevents = [], [], 0
+        for step in range(1, max_steps + 1):
+            mgr.pre_step()
+            lin(x).backward(dy)
+            x.grad = None
+            ratios.append(lin.gpu_underflow_ratio.item())
+            amax = lin.gpu_amax.item()
+            if not mgr.post_backward_sync_and_eval():
+                skips.append(step)
+            if lin.level > 0:
+                break
+        out[variant] = dict(events=list(events), ratios=ratios, skips=skips, steps=step, level=lin.level,
+                            first_amax=amax if step == 1 else None)
+    with open(os.path.join(HERE, "cfg1_variants.json"), "w") as fh:
+        json.dump(out, fh, allow_nan=True)
+
+
 if __name__ == "__main__":
-    casts()
-    underflow()
-    linear_small()
-    ladder()
-    cfg0_trajectory()
-    print("golden fixtures written to", HERE)
+    todo = _ARGS or ["casts", "underflow", "linear_small", "ladder", "cfg0_trajectory", "cfg1_variants"]
+    for name in todo:
+        globals()[name]()
+    print("golden fixtures written to", HERE, ":", ", ".join(todo))
