@@ -3,7 +3,7 @@
 The reference has no gradient synchronisation at all (its only collective is
 the overflow flag, manager.py:186-187). Data parallel training here averages
 every trainable gradient across ranks once per step. Gradients are grouped
-into flat fp32 buckets (in reverse registration order, roughly the order the
+into flat buckets (in reverse registration order, roughly the order the
 backward produces them; 64 MiB each by default: on two GPUs the char-level
 GPT ran at 6.89 ms per step with them against 7.07 ms with 5.5 MiB buckets,
 because the GEMMs leave SMs to the collective from the first bucket on).
@@ -25,9 +25,24 @@ whole-bucket reduction; on two B200s the single-layer 8192x4096x4096 step was
 slower with blocks (0.60-0.66 ms against 0.56 ms for 1024- and 2048-row
 blocks, with and without SM reserves or a CTA-capped communicator), so the
 whole-bucket reduction overlapping the input-gradient GEMM stays the default.
+
+Every trainable floating-point parameter is averaged: parameters of another
+dtype than fp32 (a bf16 LayerNorm, an fp16 embedding) get buckets of their
+own dtype. A gradient that autograd produced outside its bucket (the caller
+cleared it after ``pre_step``) is copied into the bucket view by the
+parameter's post-accumulate hook, so every rank reduces the same buffers with
+the same collectives. Gradient accumulation over several backward passes in
+one step: all but the last run inside ``no_sync()``; a second backward of the
+same parameters outside it raises, since its buckets are already reduced.
+Parameters that received no gradient on any rank in a step end it with
+``grad = None`` (as on one GPU, so the optimizer skips them): which
+parameters were ready travels as a mask in the manager's per-step telemetry
+all-reduce (``ready_mask`` / ``drop_unused``), or in its own small
+all-reduce (``sync_unused``) for callers without the manager.
 """
 from __future__ import annotations
 
+import contextlib
 from typing import Dict, List
 
 import torch
@@ -37,8 +52,9 @@ import torch.distributed as dist
 class _Bucket:
     def __init__(self, params: List[torch.nn.Parameter], device):
         self.params = params
+        self.dtype = params[0].dtype
         self.numel = sum(p.numel() for p in params)
-        self.flat = torch.zeros(self.numel, dtype=torch.float32, device=device)
+        self.flat = torch.zeros(self.numel, dtype=self.dtype, device=device)
         self.views: Dict[int, torch.Tensor] = {}
         off = 0
         for p in params:
@@ -83,7 +99,7 @@ class GradientAverager:
         # is close to the reverse of registration (module definition) order;
         # buckets are issued strictly in order, so one bucket holding an early
         # layer's gradient would hold back every bucket after it
-        trainable = {id(p) for p in mgr.get_trainable_parameters() if p.dtype == torch.float32}
+        trainable = {id(p) for p in mgr.get_trainable_parameters() if p.is_floating_point()}
         params, seen = [], set()
         for p in mgr.model.parameters():
             if id(p) in trainable and id(p) not in seen:
@@ -101,28 +117,42 @@ class GradientAverager:
                     blocks = self._row_blocks(p, reserved_sms, block_rows)
                     if len(blocks) >= 2:
                         blocked[id(p)] = (m, blocks)
+        # one bucket in the making per dtype (a bucket is one flat tensor of one
+        # dtype); flushed when full, before a row-blocked weight, and at the
+        # end in the order the dtypes first appeared
         self.buckets: List[_Bucket] = []
-        cur, cur_bytes = [], 0
+        cur: Dict[torch.dtype, list] = {}
+        cur_bytes: Dict[torch.dtype, int] = {}
+
+        def flush(dt=None):
+            for d in ([dt] if dt is not None else list(cur)):
+                if cur.get(d):
+                    self.buckets.append(_Bucket(cur[d], device))
+                cur.pop(d, None)
+                cur_bytes.pop(d, None)
+
         for p in params:
             if id(p) in blocked:
-                if cur:
-                    self.buckets.append(_Bucket(cur, device))
-                    cur, cur_bytes = [], 0
+                flush()
                 b = _Bucket([p], device)
                 b.blocks = blocked[id(p)][1]
                 self.buckets.append(b)
                 continue
-            cur.append(p)
-            cur_bytes += p.numel() * 4
-            if cur_bytes >= bucket_bytes:
-                self.buckets.append(_Bucket(cur, device))
-                cur, cur_bytes = [], 0
-        if cur:
-            self.buckets.append(_Bucket(cur, device))
+            cur.setdefault(p.dtype, []).append(p)
+            cur_bytes[p.dtype] = cur_bytes.get(p.dtype, 0) + p.numel() * p.element_size()
+            if cur_bytes[p.dtype] >= bucket_bytes:
+                flush(p.dtype)
+        flush()
         self.where = {}
         for bi, b in enumerate(self.buckets):
             for p in b.params:
                 self.where[id(p)] = bi
+        # every averaged parameter, in bucket order (the ready mask's order)
+        self.order = [p for b in self.buckets for p in b.params]
+        pin = device.type == "cuda"
+        self._mask_host = torch.zeros(max(1, len(self.order)), dtype=torch.int32, pin_memory=pin)
+        self._ready = set()            # ids of parameters marked ready in this step
+        self.accumulating = False      # inside no_sync(): gradients accumulate, nothing is reduced
         self.next = 0
         self.armed = False
         self.limited = False
@@ -171,12 +201,30 @@ class GradientAverager:
         self.next = 0
         self.ready_count = 0
         self.launch_marks = []
+        self._ready = set()
         self.armed = True
+
+    @contextlib.contextmanager
+    def no_sync(self):
+        """Backward passes inside accumulate into the buckets without reducing
+        them; the next backward outside (the step's last) marks the gradients
+        ready and starts the reductions."""
+        prev = self.accumulating
+        self.accumulating = True
+        try:
+            yield
+        finally:
+            self.accumulating = prev
 
     def _mark(self, p):
         bi = self.where.get(id(p))
-        if bi is None or not self.armed:
+        if bi is None or not self.armed or self.accumulating:
             return
+        if id(p) in self._ready:
+            raise RuntimeError(
+                "data parallel: a second backward pass produced gradients after their bucket was reduced; "
+                "run every backward pass of a step but the last inside APAManager.no_sync()")
+        self._ready.add(id(p))
         b = self.buckets[bi]
         b.pending -= 1
         self.ready_count += 1
@@ -188,7 +236,46 @@ class GradientAverager:
             self._mark(mod.bias_master)
 
     def _param_ready(self, p):
+        bi = self.where.get(id(p))
+        if self.armed and bi is not None:
+            v = self.buckets[bi].views[id(p)]
+            if p.grad is not None and p.grad.data_ptr() != v.data_ptr():
+                # produced outside the bucket (the gradient was cleared after
+                # pre_step): move it into the bucket, so that every rank
+                # reduces it with the bucket's collective
+                v.copy_(p.grad)
+                p.grad = v
         self._mark(p)
+
+    # parameters that got no gradient this step
+    def ready_mask(self) -> torch.Tensor:
+        """int32 [len(order)] host tensor: 1 where this rank produced the
+        parameter's gradient in the current step (reduce with MAX)."""
+        m = self._mask_host
+        m.zero_()
+        for i, p in enumerate(self.order):
+            if id(p) in self._ready:
+                m[i] = 1
+        return m[:len(self.order)]
+
+    def drop_unused(self, reduced) -> None:
+        """After the MAX reduction of every rank's ready_mask(): parameters no
+        rank produced a gradient for get grad None (the optimizer skips them,
+        as it does on one GPU)."""
+        for p, r in zip(self.order, reduced.tolist()):
+            if r == 0 and p.grad is not None:
+                p.grad = None
+
+    def sync_unused(self) -> None:
+        """ready_mask() reduced by its own MAX all-reduce, then drop_unused()
+        (for callers that run the averager without the manager, whose
+        telemetry reduction carries the mask)."""
+        if not self.order:
+            return
+        dev = self.buckets[0].flat.device
+        t = self.ready_mask().to(dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.pg)
+        self.drop_unused(t.cpu())
 
     def _limit_gemms(self, on: bool):
         if self.buckets and self.buckets[0].flat.is_cuda:
@@ -300,12 +387,12 @@ class GradientAverager:
                 if p.grad is None:
                     p.grad = v
                 elif p.grad.data_ptr() != v.data_ptr():
-                    # the gradient was produced outside the bucket: reduce it separately
-                    if self.avg_op is not None:
-                        dist.all_reduce(p.grad, op=self.avg_op, group=self.pg)
-                    else:
-                        dist.all_reduce(p.grad, op=dist.ReduceOp.SUM, group=self.pg)
-                        p.grad.div_(self.world)
+                    # a gradient assigned directly, not by a backward pass: it
+                    # missed its bucket's reduction, and reducing it on its own
+                    # here could make the ranks' collectives differ
+                    raise RuntimeError(
+                        f"data parallel: the gradient of a parameter of shape {tuple(p.shape)} was assigned outside "
+                        "the backward pass after pre_step, so it was not averaged")
         if self.limited:
             self._limit_gemms(False)
             self.limited = False

@@ -231,6 +231,10 @@ class _APALinearFn(torch.autograd.Function):
             _update_forensic_role(mod.weight_work, "weight", mod)
             _update_forensic_role(y, "output", mod)
 
+        if need_dw or need_db:
+            # a layer used several times in one step reports its gradients
+            # ready (to the data-parallel buckets) after its last backward
+            mod._bwd_pending += 1
         ctx.mod = mod
         ctx.level = level
         ctx.lead, ctx.M, ctx.N, ctx.K = lead, M, N, K
@@ -339,8 +343,10 @@ class _APALinearFn(torch.autograd.Function):
             _lib.check(st, "apa_colsum_finalize")
             if b.grad is None:
                 b.grad = g
-        if need_dw:
-            mod._notify_grad_ready()
+        if need_dw or need_db:
+            mod._bwd_pending -= 1
+            if mod._bwd_pending <= 0:
+                mod._notify_grad_ready()
         dx = None
         if need_dx:
             wqt = ctx.wqt
@@ -423,6 +429,7 @@ class APALinear(nn.Module):
         self._grad_epoch = -1
         self._grad_ready_cb = None
         self._dp = None                   # data-parallel gradient averager (buckets, row blocks)
+        self._bwd_pending = 0             # forwards of this step whose weight/bias backward is still to run
         self._register_load_state_dict_pre_hook(_drop_working_copy_keys)
         self.reset_parameters()
         if dev.type != "cpu":
@@ -467,6 +474,7 @@ class APALinear(nn.Module):
         if zero_pending:
             self._w_pending.zero_()
         self._epoch += 1
+        self._bwd_pending = 0
         with torch.no_grad():
             if level == LEVEL_TF32:
                 # the working weight is the master itself (stored as a plain

@@ -48,7 +48,7 @@ _REASONS = {1: "OVERFLOW", 2: "SILENT_UNDERFLOW"}
 class _LadderState:
     """Device tables for the ladder kernel, rebuilt when a buffer moves."""
 
-    def __init__(self, mgr: "APAManager", device):
+    def __init__(self, mgr: "APAManager", device, n_ready: int = 0):
         apa = list(mgr.apa_modules.values())
         oth = list(mgr.other_modules.values())
         self.L, self.O = len(apa), len(oth)
@@ -70,7 +70,12 @@ class _LadderState:
         self.ema = torch.zeros(max(self.L, 1), dtype=torch.float64, device=device)
         self.host_level: Optional[List[int]] = None
         self.host_ema: Optional[List[float]] = None
-        self.packed = torch.zeros(1 + 3 * self.L + 2 * self.O, dtype=torch.int32, device=device)
+        # data parallel: the packed telemetry the ranks MAX-reduce, followed by
+        # the gradient averager's ready mask (one word per averaged parameter)
+        self.n_ready = n_ready
+        self.ready_off = 1 + 3 * self.L + 2 * self.O
+        self.packed = torch.zeros(self.ready_off + n_ready, dtype=torch.int32, device=device)
+        self.ready_host = torch.zeros(max(1, n_ready), dtype=torch.int32, pin_memory=device.type == "cuda")
         nint = 4 + 2 * self.L + self.O
         self.dbl_off = (nint * 4 + 7) & ~7
         self.nbytes = self.dbl_off + 8 * (2 * self.L + self.O)
@@ -191,8 +196,9 @@ class APAManager:
 
     def _state(self) -> _LadderState:
         st = self._ladder
-        if st is None or st.key != self._buffer_key():
-            self._ladder = st = _LadderState(self, self._global_nonfinite.device)
+        n_ready = len(self._dp.order) if self._dp is not None else 0
+        if st is None or st.key != self._buffer_key() or st.n_ready != n_ready:
+            self._ladder = st = _LadderState(self, self._global_nonfinite.device, n_ready)
         return st
 
     # ------------------------------------------------------------------
@@ -275,7 +281,12 @@ class APAManager:
             _lib.check(lib.apa_ladder_pack(st.L, st.amax.data_ptr(), st.ratio.data_ptr(), st.flag.data_ptr(), st.O,
                                            st.oamax.data_ptr(), st.oflag.data_ptr(), st.packed.data_ptr(), s),
                        "apa_ladder_pack")
+            if st.n_ready:
+                st.packed[st.ready_off:].copy_(self._dp.ready_mask(), non_blocking=True)
             torch.distributed.all_reduce(st.packed, op=torch.distributed.ReduceOp.MAX, group=self._telemetry_group())
+            if st.n_ready:
+                # read back with the decision record (same stream, same host wait)
+                st.ready_host[: st.n_ready].copy_(st.packed[st.ready_off:], non_blocking=True)
             glob = st.packed.data_ptr()
         _lib.check(lib.apa_ladder_eval(st.L, st.amax.data_ptr(), st.ratio.data_ptr(), st.flag.data_ptr(),
                                        st.level.data_ptr(), st.ema.data_ptr(), st.O, st.oamax.data_ptr(),
@@ -421,8 +432,22 @@ class APAManager:
             avg.issue_remaining()
             join = avg.finish
         rec = self._run_ladder(before_wait=join)
+        st = self._ladder
+        if join is not None and st is not None and st.n_ready:
+            # parameters no rank produced a gradient for: grad None, as on one GPU
+            self._dp.drop_unused(st.ready_host[: st.n_ready])
         self._log_record(rec)
         return not (rec["status"] & 2)
+
+    def no_sync(self):
+        """Context for gradient accumulation under data parallelism: backward
+        passes inside it accumulate into the gradient buckets without reducing
+        them; the step's last backward runs outside it and starts the
+        reductions (a no-op context on one process)."""
+        import contextlib
+        if self._sync_gradients and self._world() > 1:
+            return self._averager().no_sync()
+        return contextlib.nullcontext()
 
     # ------------------------------------------------------------------
     # data parallel gradients

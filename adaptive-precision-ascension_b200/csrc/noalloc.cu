@@ -29,7 +29,13 @@
 // The first call on a device looks up the device address of the array (with
 // that device current) and caches it; host code never passes the array's
 // name to a kernel, since on the host that name is only a stand-in for the
-// device symbol. Make that first call before any stream capture.
+// device symbol. Make that first call before any stream capture. The cache
+// remembers the CUDA context it was taken in (the driver's context ID, unique
+// for the life of the process): when the device's context has changed since
+// (cudaDeviceReset, or a primary context released and created again), the
+// next call looks the address up again in the new context. That call is then
+// a first call again and belongs before any stream capture too.
+#include <cuda.h>
 #include <mutex>
 
 #include "apa_common.cuh"
@@ -44,17 +50,48 @@ static __device__ __align__(256) float g_bias_scratch[kScratchFloats];
 
 std::mutex g_mutex;
 float* g_device_addr[kMaxDevices] = {};
+unsigned long long g_ctx_id[kMaxDevices] = {};   // context the address belongs to (0: unknown)
 
-// Device address of g_bias_scratch on the current device, looked up once.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+// ID of the calling thread's current context, 0 when it cannot be told (no
+// current context, or a driver without cuCtxGetId).
+unsigned long long current_ctx_id() {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  if (!get_current || !get_id) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of g_bias_scratch on the current device: looked up once per
+// device, and again when the device's context is not the one it was taken in.
 int scratch_address(float** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return APA_ERR_CUDA;
   if (dev < 0 || dev >= kMaxDevices) return APA_ERR_INVALID;
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (g_device_addr[dev] == nullptr) {
+  const unsigned long long id = current_ctx_id();
+  if (g_device_addr[dev] == nullptr || (id != 0 && id != g_ctx_id[dev])) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_bias_scratch) != cudaSuccess || p == nullptr) return APA_ERR_CUDA;
     g_device_addr[dev] = static_cast<float*>(p);
+    g_ctx_id[dev] = current_ctx_id();   // the lookup made the device's context current
   }
   *out = g_device_addr[dev];
   return APA_OK;

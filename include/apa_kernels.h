@@ -269,7 +269,9 @@ int apa_tensor_stats(const void* src, int dtype, int64_t n, unsigned long long* 
  * ceil(rows / 64) * cols must not exceed 4 Mi (else APA_ERR_NOALLOC_LIMIT).
  * All calls share that array, so calls that overlap on the GPU race; the first
  * call on a device looks up the array's device address and should come before
- * any stream capture. It calls no cudaMalloc/cudaFree.
+ * any stream capture (so should the first call after the device's context was
+ * replaced, e.g. by cudaDeviceReset: the address is looked up again then). It
+ * calls no cudaMalloc/cudaFree.
  * dy_dtype: F32, F16 or BF16; work_dtype: E4M3, F16 or F32.
  */
 int apa_bias_grad_noalloc(const void* dy, int dy_dtype, int64_t rows, int64_t cols, int64_t ld,

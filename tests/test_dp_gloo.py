@@ -271,3 +271,125 @@ def test_telemetry_bit_pattern_max_two_ranks():
     for r in (0, 1):
         v = out[r]
         assert v[0] == 2.0 and math.isnan(v[1]) and v[2] == 0.25 and math.isinf(v[3]) and v[4] == 1.0
+
+
+def _run_two(worker):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return out
+
+
+class _MixedModel(nn.Module):
+    """fp32 linear layers, a bf16 LayerNorm and an fp16 scale vector, and a
+    branch (`extra`) used only when asked."""
+
+    def __init__(self):
+        super().__init__()
+        self.a = nn.Linear(6, 8)
+        self.norm = nn.LayerNorm(8).to(torch.bfloat16)
+        self.scale = nn.Parameter(torch.ones(8, dtype=torch.float16))
+        self.b = nn.Linear(8, 3)
+        self.extra = nn.Linear(8, 3)
+
+    def forward(self, x, use_extra=False):
+        h = self.norm(self.a(x).to(torch.bfloat16)).float() * self.scale.float()
+        y = self.b(h)
+        return y + self.extra(h) if use_extra else y
+
+
+def _mixed_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from apa.dp import GradientAverager
+        torch.manual_seed(0)
+        model = _MixedModel()
+        avg = GradientAverager(_FakeManager(model), None, bucket_bytes=64)
+        out = {"dtypes": sorted({str(b.dtype) for b in avg.buckets}),
+               "covered": all(id(p) in avg.where for p in model.parameters())}
+        # step 1: `extra` unused on both ranks; the caller clears the gradients
+        # after arming (zero_grad(set_to_none=True) after pre_step)
+        x = torch.randn(4, 6, generator=torch.Generator().manual_seed(rank))
+        avg.arm()
+        for p in model.parameters():
+            p.grad = None
+        model(x).pow(2).sum().backward()
+        avg.finish()
+        avg.sync_unused()
+        out["step1"] = {n: (None if p.grad is None else p.grad.float().tolist()) for n, p in model.named_parameters()}
+        out["in_bucket"] = all(p.grad is None or p.grad.data_ptr() == avg.buckets[avg.where[id(p)]].views[id(p)]
+                               .data_ptr() for p in model.parameters())
+        # step 2: `extra` used on rank 1 only
+        avg.arm()
+        model(x, use_extra=(rank == 1)).pow(2).sum().backward()
+        avg.finish()
+        avg.sync_unused()
+        out["step2_extra"] = None if model.extra.weight.grad is None else model.extra.weight.grad.tolist()
+        # the local gradients of each step, for the expected averages
+        ref = _MixedModel()
+        ref.load_state_dict(model.state_dict())
+        ref(x).pow(2).sum().backward()
+        out["local1"] = {n: p.grad.float().tolist() for n, p in ref.named_parameters() if p.grad is not None}
+        ref.zero_grad(set_to_none=True)
+        ref(x, use_extra=(rank == 1)).pow(2).sum().backward()
+        out["local2_extra"] = None if ref.extra.weight.grad is None else ref.extra.weight.grad.tolist()
+        # gradient accumulation: a second backward outside no_sync raises;
+        # inside it the micro-batches accumulate and the last one reduces
+        avg.arm()
+        model(x).sum().backward()
+        try:
+            model(x).sum().backward()
+            out["double"] = "no error"
+        except RuntimeError as e:
+            out["double"] = "raised" if "no_sync" in str(e) else str(e)
+        avg.finish()
+        avg.arm()
+        with avg.no_sync():
+            model(x).sum().backward()
+        model(2 * x).sum().backward()
+        avg.finish()
+        out["accum_a"] = model.a.weight.grad.tolist()
+        ref.zero_grad(set_to_none=True)
+        ref(x).sum().backward()
+        ref(2 * x).sum().backward()
+        out["local_accum_a"] = ref.a.weight.grad.tolist()
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_mixed_dtypes_unused_and_accumulation_two_ranks():
+    """Every trainable parameter is averaged, whatever its dtype (bf16 and fp16
+    parameters get buckets of their own); a gradient produced outside its
+    bucket (cleared after arming) is still reduced with it; a parameter no
+    rank used ends the step with grad None, one used by a single rank gets the
+    average; a second backward outside no_sync() raises, and micro-batches
+    under no_sync() accumulate before the one reduction."""
+    out = _run_two(_mixed_worker)
+    for r in (0, 1):
+        o = out[r]
+        assert o["dtypes"] == ["torch.bfloat16", "torch.float16", "torch.float32"]
+        assert o["covered"] and o["in_bucket"]
+        assert o["step1"]["extra.weight"] is None and o["step1"]["extra.bias"] is None
+        assert o["double"] == "raised"
+    for name in ("a.weight", "a.bias", "norm.weight", "norm.bias", "scale", "b.weight", "b.bias"):
+        g0, g1 = torch.tensor(out[0]["step1"][name]), torch.tensor(out[1]["step1"][name])
+        assert torch.equal(g0, g1), name                       # replicas agree
+        want = (torch.tensor(out[0]["local1"][name]) + torch.tensor(out[1]["local1"][name])) / 2
+        tol = 1e-5 if name.startswith(("a.", "b.")) else 2e-2  # bf16 / fp16 buckets
+        assert torch.allclose(g0, want, rtol=tol, atol=tol), name
+    e0, e1 = torch.tensor(out[0]["step2_extra"]), torch.tensor(out[1]["step2_extra"])
+    assert torch.equal(e0, e1) and out[0]["local2_extra"] is None
+    assert torch.allclose(e0, torch.tensor(out[1]["local2_extra"]) / 2, atol=1e-6)
+    a0 = torch.tensor(out[0]["accum_a"])
+    want = (torch.tensor(out[0]["local_accum_a"]) + torch.tensor(out[1]["local_accum_a"])) / 2
+    assert torch.equal(a0, torch.tensor(out[1]["accum_a"])) and torch.allclose(a0, want, atol=1e-5)

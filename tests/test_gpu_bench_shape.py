@@ -186,7 +186,8 @@ def test_epilogues_bit_exact_on_bench_inputs(L, rung):
     L.check(L.lib().apa_linear_wgrad_block(rung, dyqt.data_ptr(), M, xqt.data_ptr(), M, dw.data_ptr(), K, M, N, K, 0,
                                            cnt.data_ptr(), rmax.data_ptr(), 0, L.stream_handle()), "wgrad block")
     torch.cuda.synchronize()
-    assert np.array_equal(dw.cpu().numpy(), O.quantize(seen, WD[rung]))
+    # |dW| reaches ~480 here: above 464 the E4M3 rounding gives NaN (the reference's cast rule)
+    assert np.array_equal(dw.cpu().numpy(), O.quantize(seen, WD[rung]), equal_nan=True)
     if rung != 2:
         nz, uf = O.underflow_counts(seen, O.THRESHOLDS_MIN[rung])
         assert cnt.cpu().tolist() == [nz, uf, 0]
