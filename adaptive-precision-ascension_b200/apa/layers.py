@@ -296,12 +296,14 @@ class _APALinearFn(torch.autograd.Function):
                 g = dp.grad_view(W) if dp is not None else None
                 if g is None:
                     g = torch.empty_like(W)
-            # small weight gradients over long token counts are split along the
-            # tokens (two kernels, fp32 partial sums in a scratch buffer)
+            # scratch for the weight gradient: small gradients over long token
+            # counts are split along the tokens (two kernels, fp32 partial sums),
+            # and a last, partial wave of tiles is split along the tokens too
+            # (stream-K: the splits' partials are added by the last to finish)
             nbytes = ctypes.c_int64(0)
             _lib.check(lib.apa_wgrad_workspace_bytes(level, M, N, K, ctypes.addressof(nbytes)),
                        "apa_wgrad_workspace_bytes")
-            blocks = dp.weight_blocks(mod, g) if (dp is not None and nbytes.value == 0 and not accumulate) else None
+            blocks = dp.weight_blocks(mod, g) if (dp is not None and not accumulate) else None
             if blocks:
                 # data parallel: rows of the gradient in blocks, each block's
                 # all-reduce issued as soon as its rows are written

@@ -117,8 +117,53 @@ struct EpiArgs {
   int splits;                       // split-K: K blocks divided into this many units per tile
   int kb_per_split;                 // 128-byte K slabs per split
   int split_rows;                   // output row offset between the splits' slices
+  // stream-K tail: tiles from sk_first on (the last, partial wave) are split
+  // along K into sk_splits = 2 units that run in the same wave; each
+  // epilogue warp stores its raw partial to sk_ws and takes a ticket, and the
+  // warp that finishes second adds the other partial and applies the
+  // epilogue. sk_splits < 2: no tail split.
+  float* sk_ws;                     // [tail tile][split][cta][epi warp][cols/4][32 lanes][4] fp32
+  int* sk_tickets;                  // [tail tile][cta][epi warp], zero on entry and on exit
+  int64_t sk_ws_bytes;              // caller workspace available (partials + tickets)
+  int sk_first, sk_splits, sk_kb_per_split;
   int M, N, K;
 };
+
+// One work unit of the persistent schedule: an output tile and the range of
+// 128-byte K slabs it reduces. sk_split >= 0 marks a stream-K tail unit;
+// orow is the output row offset of a split-K slice.
+struct Unit {
+  int tile, kb0, kb1, sk_split, orow;
+};
+
+__host__ __device__ __forceinline__ int num_work_units(const EpiArgs& ea, int num_tiles) {
+  if (ea.sk_splits > 1) return ea.sk_first + (num_tiles - ea.sk_first) * ea.sk_splits;
+  return num_tiles * (ea.splits > 1 ? ea.splits : 1);
+}
+
+__device__ __forceinline__ Unit unit_of(const EpiArgs& ea, int w, int kb_count) {
+  Unit u;
+  u.sk_split = -1;
+  u.orow = 0;
+  if (ea.sk_splits > 1 && w >= ea.sk_first) {
+    const int v = w - ea.sk_first;
+    u.tile = ea.sk_first + v / ea.sk_splits;
+    u.sk_split = v - (v / ea.sk_splits) * ea.sk_splits;
+    u.kb0 = u.sk_split * ea.sk_kb_per_split;
+    u.kb1 = min(u.kb0 + ea.sk_kb_per_split, kb_count);
+  } else if (ea.splits > 1) {
+    u.tile = w / ea.splits;
+    const int sp = w - u.tile * ea.splits;
+    u.kb0 = sp * ea.kb_per_split;
+    u.kb1 = min(u.kb0 + ea.kb_per_split, kb_count);
+    u.orow = sp * ea.split_rows;
+  } else {
+    u.tile = w;
+    u.kb0 = 0;
+    u.kb1 = kb_count;
+  }
+  return u;
+}
 
 // ---------------------------------------------------------------------------
 // PTX wrappers
@@ -630,9 +675,8 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
   const int num_m = (ea.M + C::kTileM - 1) / C::kTileM;
   const int num_tiles = num_m * num_n;
   const int kb_count = (int)(((int64_t)ea.K * KindInfo<KIND>::bytes + kSlab - 1) / kSlab);
-  // work units: (tile, K split); one split covers the whole K range
-  const int splits = ea.splits > 1 ? ea.splits : 1;
-  const int num_units = num_tiles * splits;
+  // work units: (tile, K range)
+  const int num_units = num_work_units(ea, num_tiles);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -670,11 +714,10 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int w = unit0; ok && w < num_units; w += units) {
-        const int tile = w / splits, split = w - tile * splits;
-        const int kb0 = splits > 1 ? split * ea.kb_per_split : 0;
-        const int kb1 = splits > 1 ? min(kb0 + ea.kb_per_split, kb_count) : kb_count;
+        const Unit un = unit_of(ea, w, kb_count);
+        const int kb0 = un.kb0, kb1 = un.kb1;
         int m_blk, n_blk;
-        tile_coords(tile, num_m, num_n, kGroup, m_blk, n_blk);
+        tile_coords(un.tile, num_m, num_n, kGroup, m_blk, n_blk);
         const int a_row = m_blk * C::kTileM + (int)rank * BM;
         const int b_row = n_blk * BN + (int)rank * C::kBRows;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -709,9 +752,8 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
       bool ok = true;
       constexpr uint32_t id = idesc<KIND, BN, C::kTileM>();
       for (int w = unit0; ok && w < num_units; w += units, ++local) {
-        const int split = w - (w / splits) * splits;
-        const int kb0 = splits > 1 ? split * ea.kb_per_split : 0;
-        const int kb1 = splits > 1 ? min(kb0 + ea.kb_per_split, kb_count) : kb_count;
+        const Unit un = unit_of(ea, w, kb_count);
+        const int kb0 = un.kb0, kb1 = un.kb1;
         const int acc = local & 1;
         const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
         if (!mbar_wait<PAIR>(&tempty[acc], acc_par ^ 1u, kStatusTimeoutAcc)) { ok = false; break; }
@@ -757,8 +799,9 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
       }
     };
     for (int w = unit0; w < num_units; w += units, ++local) {
-      const int tile = w / splits, split = w - tile * splits;
-      const int orow_off = split * ea.split_rows;   // this split's slice of the output
+      const Unit un = unit_of(ea, w, kb_count);
+      const int tile = un.tile;
+      const int orow_off = un.orow;   // this split's slice of the output (split-K)
       const int acc = local & 1;
       const uint32_t acc_par = (uint32_t)(local >> 1) & 1u;
       int m_blk, n_blk;
@@ -785,6 +828,45 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
       const uint32_t tbase =
           tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN) + (uint32_t)(part * C::kWarpCols);
       bool released = false;
+      // stream-K tail unit (two splits): store this split's raw partial
+      // (lane-major, so each warp store writes 512 contiguous bytes), then
+      // take the ticket of this warp's part of the tile; the warp that takes
+      // the second ticket adds the other split's partial to its own and runs
+      // the epilogue. fp32 addition commutes, so the sum has the same bits
+      // whichever split finishes last.
+      const float4* sk_other = nullptr;   // set: this warp finishes the tile
+      if (un.sk_split >= 0) {
+        constexpr int kChunk4 = C::kWarpCols * 8;   // float4s per warp and split (kWarpCols x 32 lanes / 4)
+        const int tail = tile - ea.sk_first;
+        const int64_t widx = (int64_t)rank * kEpiWarps + e;
+        const int64_t per_split = (int64_t)C::kCtas * kEpiWarps;
+        float4* mine = reinterpret_cast<float4*>(ea.sk_ws) +
+                       (((int64_t)tail * 2 + un.sk_split) * per_split + widx) * kChunk4 + lane;
+#pragma unroll 1
+        for (int u = 0; u < kUnits; ++u) {
+          if (col_base + u * 64 >= ea.N) break;   // warp-uniform
+          uint32_t r[64];
+          tmem_ld32_nowait(tbase + (uint32_t)(u * 64), r);
+          tmem_ld32_nowait(tbase + (uint32_t)(u * 64 + 32), r + 32);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c4 = 0; c4 < 16; ++c4)
+            mine[(u * 16 + c4) * 32] = make_float4(fu(r[4 * c4]), fu(r[4 * c4 + 1]), fu(r[4 * c4 + 2]),
+                                                   fu(r[4 * c4 + 3]));
+        }
+        __threadfence();
+        __syncwarp();
+        int old = 0;
+        if (lane == 0) old = atomicAdd(&ea.sk_tickets[(int64_t)tail * per_split + widx], 1);
+        old = __shfl_sync(0xFFFFFFFFu, old, 0);
+        if (old == 0) {
+          release_acc(acc);   // the other split's warp finishes this part of the tile
+          continue;
+        }
+        __threadfence();
+        sk_other = reinterpret_cast<const float4*>(ea.sk_ws) +
+                   (((int64_t)tail * 2 + (1 - un.sk_split)) * per_split + widx) * kChunk4 + lane;
+      }
 #pragma unroll 1
       for (int u = 0; u < kUnits; ++u) {
         const int col0 = col_base + u * 64;
@@ -798,6 +880,16 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
           // every TMEM read of this warp's part of the accumulator is done
           release_acc(acc);
           released = true;
+        }
+        if (sk_other != nullptr) {
+#pragma unroll
+          for (int c4 = 0; c4 < 16; ++c4) {
+            const float4 v = __ldcg(sk_other + (u * 16 + c4) * 32);
+            r[4 * c4] = __float_as_uint(fu(r[4 * c4]) + v.x);
+            r[4 * c4 + 1] = __float_as_uint(fu(r[4 * c4 + 1]) + v.y);
+            r[4 * c4 + 2] = __float_as_uint(fu(r[4 * c4 + 2]) + v.z);
+            r[4 * c4 + 3] = __float_as_uint(fu(r[4 * c4 + 3]) + v.w);
+          }
         }
         epi_unit<KIND, EPI>(ea, sb + u * 64, r, st, check, row_ok, nv);
         if (ea.coalesced_out) {
@@ -998,6 +1090,41 @@ int pair_capacity() {
   return clusters;
 }
 
+// Stream-K split of the last, partial wave: with `tiles` tiles on `slots`
+// CTAs (or CTA pairs), W full waves and R < slots left over, the R tail
+// tiles are each split along K into two units (at least 8 slabs each) that
+// run side by side, so the tail costs about half a tile instead of a whole
+// one. Only when the tail fills at most half a wave. Workspace: 2 R fp32 tile
+// partials, then one int ticket per tail tile, CTA and epilogue warp.
+struct TailPlan {
+  int first, splits, kb_per_split;
+  int64_t part_bytes, bytes;
+};
+
+inline TailPlan tail_plan(int64_t tiles, int64_t slots, int64_t kb_count, int64_t tile_elems, int ctas_x_warps) {
+  TailPlan t{0, 0, 0, 0, 0};
+  if (slots < 2 || tiles < slots) return t;
+  const int64_t W = tiles / slots, R = tiles - W * slots;
+  if (R == 0 || 2 * R > slots) return t;
+  if (kb_count < 16) return t;
+  const int64_t S = 2;
+  const int64_t per = (kb_count + 1) / 2;
+  t.first = (int)(W * slots);
+  t.splits = (int)S;
+  t.kb_per_split = (int)per;
+  t.part_bytes = R * S * tile_elems * 4;
+  t.bytes = t.part_bytes + (R * ctas_x_warps * 4 + 15) / 16 * 16;
+  return t;
+}
+
+template <int BN, bool PAIR, int EW>
+TailPlan tail_plan_for(const EpiArgs& ea, int kind_bytes, int64_t slots) {
+  using C = Cfg<BN, PAIR, EW>;
+  const int64_t tiles = ((int64_t)(ea.M + C::kTileM - 1) / C::kTileM) * ((ea.N + BN - 1) / BN);
+  const int64_t kb_count = ((int64_t)ea.K * kind_bytes + kSlab - 1) / kSlab;
+  return tail_plan(tiles, slots, kb_count, (int64_t)C::kTileM * BN, C::kCtas * EW);
+}
+
 template <int KIND, int BN, int EPI, bool PAIR, int EW>
 int launch_t(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea, int grid_cap, cudaStream_t s) {
   using C = Cfg<BN, PAIR, EW>;
@@ -1020,12 +1147,29 @@ int launch_t(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea,
   ea.tma_out = make_out_map(&to, ea) ? 1 : 0;
   ea.coalesced_out = (!ea.tma_out && ea.accumulate && ea.vec_out) ? 1 : 0;
   // work units: tiles x K splits
-  const int tiles = ((ea.M + C::kTileM - 1) / C::kTileM) * ((ea.N + BN - 1) / BN) * (ea.splits > 1 ? ea.splits : 1);
+  int tiles = ((ea.M + C::kTileM - 1) / C::kTileM) * ((ea.N + BN - 1) / BN) * (ea.splits > 1 ? ea.splits : 1);
+  // stream-K tail (caller workspace given, no split-K): planned against the
+  // number of CTAs (pairs) that actually run
+  auto plan_tail = [&](int64_t slots) -> int {
+    ea.sk_splits = 0;
+    if (ea.sk_ws == nullptr || ea.splits > 1) return APA_OK;
+    const TailPlan tp = tail_plan_for<BN, PAIR, EW>(ea, KindInfo<KIND>::bytes, slots);
+    if (tp.splits < 2 || tp.bytes > ea.sk_ws_bytes) return APA_OK;
+    ea.sk_first = tp.first;
+    ea.sk_splits = tp.splits;
+    ea.sk_kb_per_split = tp.kb_per_split;
+    ea.sk_tickets = reinterpret_cast<int*>(reinterpret_cast<char*>(ea.sk_ws) + tp.part_bytes);
+    if (cudaMemsetAsync(ea.sk_tickets, 0, (size_t)(tp.bytes - tp.part_bytes), s) != cudaSuccess) return APA_ERR_CUDA;
+    tiles = num_work_units(ea, tiles);
+    return APA_OK;
+  };
   if constexpr (PAIR) {
     const int cap = pair_capacity<KIND, BN, EPI, EW>();
     if (cap < 1) return APA_ERR_UNSUPPORTED;
-    int clusters = std::min(tiles, grid_cap > 0 ? std::max(1, grid_cap / 2) : cap);
-    clusters = std::max(1, std::min(clusters, cap));
+    const int slots = std::max(1, std::min(grid_cap > 0 ? std::max(1, grid_cap / 2) : cap, cap));
+    if (int st = plan_tail(slots)) return st;
+    int clusters = std::min(tiles, slots);
+    clusters = std::max(1, clusters);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters, 1, 1);
     cfg.blockDim = dim3(C::kThreads, 1, 1);
@@ -1041,7 +1185,9 @@ int launch_t(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea,
     if (cudaLaunchKernelEx(&cfg, gemm_kernel<KIND, BN, EPI, true, EW>, ta, tb, to, ea) != cudaSuccess)
       return APA_ERR_CUDA;
   } else {
-    int grid = std::min(tiles, grid_cap > 0 ? grid_cap : num_sms());
+    const int slots = std::max(1, grid_cap > 0 ? grid_cap : num_sms());
+    if (int st = plan_tail(slots)) return st;
+    int grid = std::min(tiles, slots);
     if (grid < 1) grid = 1;
     gemm_kernel<KIND, BN, EPI, false, EW><<<grid, C::kThreads, C::kSmemBytes, s>>>(ta, tb, to, ea);
   }
@@ -1206,7 +1352,8 @@ struct GemmPlan {
 // deeper operand pipeline, also when each CTA runs only one or two tiles
 // (measured on 8192 x 1024 x 4096: FP8 forward 31.5 against 35.0 µs, FP16
 // input gradient 67 against 76 µs).
-GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int es, int out_es, int slots, bool pair_possible, int tile) {
+GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int es, int out_es, int slots, bool pair_possible, int tile,
+                   int epi) {
   using namespace gemm;
   auto cdiv = [](int64_t a, int64_t b) { return (a + b - 1) / b; };
   const int64_t sms = std::max(1, slots);
@@ -1226,7 +1373,12 @@ GemmPlan plan_gemm(int64_t M, int64_t N, int64_t K, int es, int out_es, int slot
     if (pair_possible && M > 128) {
       const int64_t w = cdiv(tilesP, pairs);
       const bool long_k = k_bytes >= 512 * (int64_t)kSlab;
-      const double gain = (!epi_bound && (w >= 3 || long_k)) ? 1.0 / 1.08 : 1.0 / 0.97;
+      // an epilogue-bound forward GEMM (fp32 output, telemetry) measured
+      // 10-12 % faster on the pair with eight epilogue warps at equal wave
+      // counts (8192 tokens x 1024 -> 3072 / 4096: 35.8 against 40.8 µs,
+      // 41.5 against 47.1 µs); epilogue-bound input gradients did not
+      const double gain = (!epi_bound && (w >= 3 || long_k)) ? 1.0 / 1.08
+                          : (epi_bound && epi == EPI_FWD) ? 0.9 : 1.0 / 0.97;
       const double tp = (double)w * width(256) * gain;
       if (tp < best) { best = tp; tile = kTilePair; }
     }
@@ -1269,7 +1421,7 @@ int resolve_plan(int rung, int epi, int64_t M, int64_t N, int64_t K, int out_dt,
   if (tile == kTilePair && !pair) return APA_ERR_UNSUPPORTED;
   const int es = rung == APA_RUNG_FP8 ? 1 : rung == APA_RUNG_FP16 ? 2 : 4;
   const int out_es = out_dt == APA_DT_F32 ? 4 : 2;
-  GemmPlan pl = plan_gemm(M, N, K, es, out_es, grid_cap > 0 ? grid_cap : num_sms(), pair, tile);
+  GemmPlan pl = plan_gemm(M, N, K, es, out_es, grid_cap > 0 ? grid_cap : num_sms(), pair, tile, epi);
   if (ew_flag == kEpiFlag4) pl.ew = 4;
   if (ew_flag == kEpiFlag8) pl.ew = 8;
   *out = pl;
@@ -1297,6 +1449,53 @@ int gemm_dispatch(int rung, int epi, const void* A, int64_t lda, const void* B, 
 #undef APA_EPI_CASE
 }
 
+// Clusters of the pair kernel that fit on the device.
+template <int KIND, int EPI>
+int cap_of(int ew) {
+  using namespace gemm;
+  return ew == 8 ? pair_capacity<KIND, 256, EPI, 8>() : pair_capacity<KIND, 256, EPI, 4>();
+}
+
+// Workspace the stream-K tail of this GEMM would use with the launch
+// configuration gemm_dispatch picks now (0 when the last wave is full or
+// more than half full).
+int tail_workspace_bytes(int rung, int epi, const gemm::EpiArgs& ea, int64_t* bytes_out) {
+  using namespace gemm;
+  *bytes_out = 0;
+  GemmPlan pl;
+  if (int st = resolve_plan(rung, epi, ea.M, ea.N, ea.K, ea.out_dt, 0, 0, &pl)) return st;
+  const int grid_cap = g_gemm_sm_limit;
+  const int kb = rung == APA_RUNG_FP8 ? 1 : rung == APA_RUNG_FP16 ? 2 : 4;
+  TailPlan tp{0, 0, 0, 0, 0};
+  if (pl.tile == kTilePair) {
+    int cap = 0;
+#define APA_CAP_CASE(KIND)                                                                                  \
+  switch (epi) {                                                                                             \
+    case EPI_FWD: cap = cap_of<KIND, EPI_FWD>(pl.ew); break;                                           \
+    case EPI_DGRAD: cap = cap_of<KIND, EPI_DGRAD>(pl.ew); break;                                       \
+    case EPI_RAW: cap = cap_of<KIND, EPI_RAW>(pl.ew); break;                                           \
+    default: cap = cap_of<KIND, EPI_WGRAD>(pl.ew);                                                     \
+  }
+    switch (rung) {
+      case APA_RUNG_FP8: APA_CAP_CASE(KIND_E4M3) break;
+      case APA_RUNG_FP16: APA_CAP_CASE(KIND_F16) break;
+      default: APA_CAP_CASE(KIND_TF32)
+    }
+#undef APA_CAP_CASE
+    if (cap < 1) return APA_OK;
+    const int slots = std::max(1, std::min(grid_cap > 0 ? std::max(1, grid_cap / 2) : cap, cap));
+    tp = pl.ew == 8 ? tail_plan_for<256, true, 8>(ea, kb, slots) : tail_plan_for<256, true, 4>(ea, kb, slots);
+  } else {
+    const int slots = std::max(1, grid_cap > 0 ? grid_cap : num_sms());
+    if (pl.tile == kTile256)
+      tp = pl.ew == 8 ? tail_plan_for<256, false, 8>(ea, kb, slots) : tail_plan_for<256, false, 4>(ea, kb, slots);
+    else
+      tp = pl.ew == 8 ? tail_plan_for<128, false, 8>(ea, kb, slots) : tail_plan_for<128, false, 4>(ea, kb, slots);
+  }
+  *bytes_out = tp.splits > 1 ? tp.bytes : 0;
+  return APA_OK;
+}
+
 }  // namespace apa
 
 using apa::gemm::EpiArgs;
@@ -1315,6 +1514,8 @@ EpiArgs blank(int64_t M, int64_t N, int64_t K) {
   ea.bias = nullptr; ea.amax = nullptr; ea.flag = nullptr;
   ea.counters = nullptr; ea.ratio_max = nullptr; ea.vmin = 0.0f; ea.accumulate = 0; ea.finalize = 1; ea.telem = 0;
   ea.splits = 1; ea.kb_per_split = 0; ea.split_rows = 0;
+  ea.sk_ws = nullptr; ea.sk_tickets = nullptr; ea.sk_ws_bytes = 0;
+  ea.sk_first = 0; ea.sk_splits = 0; ea.sk_kb_per_split = 0;
   ea.M = (int)M; ea.N = (int)N; ea.K = (int)K;
   return ea;
 }
@@ -1355,6 +1556,27 @@ extern "C" int apa_linear_dgrad(int rung, const void* dyq, int64_t lddy, const v
                             static_cast<cudaStream_t>(stream));
 }
 
+namespace {
+
+// The weight-gradient GEMM with its fused epilogue; `ws` (nullable, 16-byte
+// aligned) lets the last partial wave of tiles be split along K (stream-K).
+int wgrad_gemm(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt, float* dw, int64_t lddw,
+               int64_t M, int64_t N, int64_t K, int accumulate, unsigned long long* counters, float* ratio_max,
+               void* ws, int64_t ws_bytes, cudaStream_t s) {
+  EpiArgs ea = blank(N, K, M);
+  ea.out = dw; ea.ldo = lddw; ea.out_dt = APA_DT_F32; ea.vec_out = out_vec(dw, lddw, 4);
+  ea.accumulate = accumulate; ea.counters = counters; ea.ratio_max = ratio_max;
+  ea.telem = counters ? 1 : 0;
+  ea.vmin = rung == APA_RUNG_FP8 ? 0.015625f : rung == APA_RUNG_FP16 ? 6.1035e-5f : 0.0f;
+  if (ws != nullptr && ws_bytes > 0 && (reinterpret_cast<uintptr_t>(ws) & 15u) == 0) {
+    ea.sk_ws = static_cast<float*>(ws);
+    ea.sk_ws_bytes = ws_bytes;
+  }
+  return apa::gemm_dispatch(rung, apa::gemm::EPI_WGRAD, dyqt, lddyt, xqt, ldxt, ea, 0, 0, s);
+}
+
+}  // namespace
+
 extern "C" int apa_linear_wgrad(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt, float* dw,
                                 int64_t lddw, int64_t M, int64_t N, int64_t K, int accumulate,
                                 unsigned long long* counters, float* ratio_max, void* stream) {
@@ -1363,13 +1585,8 @@ extern "C" int apa_linear_wgrad(int rung, const void* dyqt, int64_t lddyt, const
   if (int st = check_dims(N, K, M)) return st;
   if (!dyqt || !xqt || !dw || lddw < K || lddyt < M || ldxt < M) return APA_ERR_INVALID;
   if (rung != APA_RUNG_TF32 && !counters) return APA_ERR_INVALID;
-  EpiArgs ea = blank(N, K, M);
-  ea.out = dw; ea.ldo = lddw; ea.out_dt = APA_DT_F32; ea.vec_out = out_vec(dw, lddw, 4);
-  ea.accumulate = accumulate; ea.counters = counters; ea.ratio_max = ratio_max;
-  ea.telem = counters ? 1 : 0;
-  ea.vmin = rung == APA_RUNG_FP8 ? 0.015625f : rung == APA_RUNG_FP16 ? 6.1035e-5f : 0.0f;
-  return apa::gemm_dispatch(rung, apa::gemm::EPI_WGRAD, dyqt, lddyt, xqt, ldxt, ea, 0, 0,
-                            static_cast<cudaStream_t>(stream));
+  return wgrad_gemm(rung, dyqt, lddyt, xqt, ldxt, dw, lddw, M, N, K, accumulate, counters, ratio_max, nullptr, 0,
+                    static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int apa_linear_wgrad_block(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt,
@@ -1437,7 +1654,7 @@ SplitPlan plan_wgrad_split(int rung, int64_t Mo, int64_t No, int64_t Kt) {
   SplitPlan sp{0, 0, 1, 0, 0, 0};
   const int es = rung == APA_RUNG_FP8 ? 1 : rung == APA_RUNG_FP16 ? 2 : 4;
   const int slots = g_gemm_sm_limit > 0 ? g_gemm_sm_limit : num_sms();
-  GemmPlan pl = plan_gemm(Mo, No, Kt, es, 4, slots, false, 0);
+  GemmPlan pl = plan_gemm(Mo, No, Kt, es, 4, slots, false, 0, gemm::EPI_WGRAD);
   auto cdiv = [](int64_t a, int64_t b) { return (a + b - 1) / b; };
   const int64_t tiles = cdiv(Mo, 128) * cdiv(No, pl.tile == kTile128 ? 128 : 256);
   const int64_t kb_count = cdiv(Kt * es, kSlab);
@@ -1463,8 +1680,14 @@ extern "C" int apa_wgrad_workspace_bytes(int rung, int64_t M, int64_t N, int64_t
   if (int st = check_dims(N, K, M)) return st;
   if (rung != APA_RUNG_FP8 && rung != APA_RUNG_FP16 && rung != APA_RUNG_TF32) return APA_ERR_INVALID;
   const apa::SplitPlan sp = apa::plan_wgrad_split(rung, N, K, M);
-  *bytes_out = sp.splits > 1 ? (int64_t)sp.splits * sp.rows_pad * sp.ld_ws * 4 : 0;
-  return APA_OK;
+  if (sp.splits > 1) {
+    *bytes_out = (int64_t)sp.splits * sp.rows_pad * sp.ld_ws * 4;
+    return APA_OK;
+  }
+  // otherwise the stream-K split of the last partial wave, if it has one
+  EpiArgs ea = blank(N, K, M);
+  ea.out_dt = APA_DT_F32;
+  return apa::tail_workspace_bytes(rung, apa::gemm::EPI_WGRAD, ea, bytes_out);
 }
 
 extern "C" int apa_linear_wgrad_ws(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt, float* dw,
@@ -1480,8 +1703,8 @@ extern "C" int apa_linear_wgrad_ws(int rung, const void* dyqt, int64_t lddyt, co
   // (the plan only splits outputs of a few tiles, so neither limit is reached)
   if (need == 0 || !workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15u) ||
       N * K >= (1ll << 31) || sp.splits > 8)
-    return apa_linear_wgrad(rung, dyqt, lddyt, xqt, ldxt, dw, lddw, M, N, K, accumulate, counters, ratio_max,
-                            stream);
+    return wgrad_gemm(rung, dyqt, lddyt, xqt, ldxt, dw, lddw, M, N, K, accumulate, counters, ratio_max, workspace,
+                      workspace_bytes, static_cast<cudaStream_t>(stream));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // phase 1: raw fp32 partial sums, one slice per split
   EpiArgs ea = blank(N, K, M);

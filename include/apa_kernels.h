@@ -172,7 +172,8 @@ int apa_linear_wgrad_block(int rung, const void* dyqt, int64_t lddyt, const void
 
 /*
  * Scratch bytes apa_linear_wgrad_ws uses for this shape (same M, N, K as
- * apa_linear_wgrad), 0 when the weight gradient is not split.
+ * apa_linear_wgrad), 0 when the weight gradient is not split (neither along
+ * the tokens for a small gradient, nor in its last partial wave of tiles).
  */
 int apa_wgrad_workspace_bytes(int rung, int64_t M, int64_t N, int64_t K, int64_t* bytes_out);
 
@@ -183,8 +184,14 @@ int apa_wgrad_workspace_bytes(int rung, int64_t M, int64_t N, int64_t K, int64_t
  * split into up to 8 parts computed in parallel as fp32 partial sums, then
  * summed in split order by a second kernel that applies the same epilogue
  * (underflow counts, rounding to the working dtype, overwrite or accumulate,
- * ratio fold). Without enough scratch it behaves exactly like
- * apa_linear_wgrad. Same reference interfaces as apa_linear_wgrad.
+ * ratio fold). Otherwise, when the persistent schedule's last wave of tiles is
+ * at most half full (e.g. 4096 x 4096 over 8192 tokens: 256 tiles on 74 CTA
+ * pairs), each tile of that wave is split in two along the tokens (stream-K):
+ * both halves run side by side, store their fp32 partial sums in the scratch
+ * buffer, and the half that finishes second adds the two (the same bits
+ * whichever finishes first) and applies the epilogue. The entry point clears
+ * the scratch words it needs itself. Without enough scratch it behaves exactly
+ * like apa_linear_wgrad. Same reference interfaces as apa_linear_wgrad.
  */
 int apa_linear_wgrad_ws(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt,
                         float* dw, int64_t lddw, int64_t M, int64_t N, int64_t K, int accumulate,
