@@ -49,6 +49,9 @@ SIGNATURES = {
     "apa_adamw_cast": [_VP, _VP, _VP, _VP, _I64, _I64, _I64, _F, _F, _F, _F, _F, _I64, _VP, _I, _I64, _VP, _I64,
                        _VP, _VP],
     "apa_bias_grad_noalloc": [_VP, _I, _I64, _I64, _I64, _I, _VP, _I, _VP],
+    "apa_dp_signal": [_VP, _VP],
+    "apa_dp_allreduce": [_VP, _I64, _I, _I, _VP, _VP, _VP, _I, _VP],
+    "apa_dp_wait": [_VP, _VP, _I, _I, _VP],
     "apa_ladder_pack": [_I, _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP],
     "apa_ladder_eval": [_I, _VP, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _I64, _I64,
                         ctypes.c_double, ctypes.c_double, _VP, _VP, _VP],

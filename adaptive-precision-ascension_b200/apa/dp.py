@@ -39,6 +39,11 @@ Parameters that received no gradient on any rank in a step end it with
 parameters were ready travels as a mask in the manager's per-step telemetry
 all-reduce (``ready_mask`` / ``drop_unused``), or in its own small
 all-reduce (``sync_unused``) for callers without the manager.
+
+APALinear weights of 1 Mi elements or more skip the NCCL buckets when the
+GPUs support NVLink multicast: their gradients are averaged through NVLink
+SHARP by the library's own kernels (``_NvlsGradients``), each as soon as its
+weight-gradient GEMM has written it.
 """
 from __future__ import annotations
 
@@ -85,9 +90,98 @@ def _capped_nccl_group(process_group, max_ctas: int):
     return dist.new_group(ranks=ranks, backend="nccl", pg_options=opts, use_local_synchronization=True)
 
 
+class _NvlsGradients:
+    """APALinear weight gradients averaged through NVLink SHARP instead of
+    NCCL: the fp32 gradients of the chosen weights live in one symmetric
+    allocation bound to an NVLink multicast object (each weight's `.grad` is a
+    view into it, so the weight-gradient kernel writes there); after a
+    weight's gradient is written, apa_dp_signal releases it to every rank and,
+    on a side stream, apa_dp_allreduce averages this rank's 1/world shard of
+    it through the switch (multimem.ld_reduce, multimem.st back to every
+    rank) and apa_dp_wait holds the stream until every shard is in. Per GPU
+    and gradient of B bytes about 2 B / world cross NVLink, against
+    2 (world - 1) / world B for a ring all-reduce, and the reduction starts
+    as soon as that one gradient exists.
+
+    Every rank must reduce these gradients in every step: a rank whose layer
+    produced no gradient contributes zeros (finish() launches its reduction);
+    a rank that skips the step altogether makes the others' bounded waits
+    expire, which the next ladder decision reports as an error."""
+
+    def __init__(self, params, pg, world: int, rank: int, device, ctas: int):
+        import torch.distributed._symmetric_memory as symm
+        self.world, self.rank, self.ctas = world, rank, ctas
+        self.index: Dict[int, int] = {}
+        self.offset: Dict[int, int] = {}
+        off = 0
+        for i, p in enumerate(params):
+            self.index[id(p)] = i
+            self.offset[id(p)] = off
+            off += (p.numel() + 63) // 64 * 64          # 256-byte aligned gradients
+        self.ctr_off = off                              # per gradient: ready, done, epoch, pad (u32)
+        total = off + 4 * len(params)
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        if not symm._SymmetricMemory.has_multicast_support(symm.DeviceType.CUDA, idx):
+            raise RuntimeError("no NVLink multicast support")
+        buf = symm.empty(total, dtype=torch.float32, device=device)
+        group = pg if pg is not None else dist.group.WORLD
+        hdl = symm.rendezvous(buf, group)
+        if not int(hdl.multicast_ptr):
+            raise RuntimeError("no multicast mapping for the gradient buffer")
+        base_local = int(hdl.buffer_ptrs[hdl.rank])
+        self.mc = int(hdl.multicast_ptr) + (buf.data_ptr() - base_local)
+        self.buf, self.hdl = buf, hdl
+        buf.zero_()
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)
+        self.views = {id(p): buf[self.offset[id(p)]:self.offset[id(p)] + p.numel()].view_as(p) for p in params}
+        self.params = list(params)
+        self.stream = None
+        self.pending = False
+
+    def _ctr(self, i: int, word: int, multicast: bool) -> int:
+        byte = (self.ctr_off + 4 * i + word) * 4
+        return (self.mc if multicast else self.buf.data_ptr()) + byte
+
+    def reduce(self, p) -> None:
+        """Average p's gradient over the ranks (queued; see join)."""
+        from . import _lib
+        lib = _lib.lib()
+        i = self.index[id(p)]
+        dev = self.buf.device
+        cur = torch.cuda.current_stream(dev)
+        _lib.check(lib.apa_dp_signal(self._ctr(i, 0, True), _lib.stream_handle(dev)), "apa_dp_signal")
+        if self.stream is None:
+            self.stream = torch.cuda.Stream(device=dev)
+        self.stream.wait_stream(cur)
+        sh = self.stream.cuda_stream
+        _lib.check(lib.apa_dp_allreduce(self.mc + self.offset[id(p)] * 4, p.numel(), self.world, self.rank,
+                                        self._ctr(i, 0, False), self._ctr(i, 1, True), self._ctr(i, 2, False),
+                                        self.ctas, sh), "apa_dp_allreduce")
+        _lib.check(lib.apa_dp_wait(self._ctr(i, 1, False), self._ctr(i, 2, False), self.world, self.ctas, sh),
+                   "apa_dp_wait")
+        self.pending = True
+
+    def join(self, stream) -> None:
+        if self.pending:
+            stream.wait_stream(self.stream)
+            self.pending = False
+
+
+def _nvls_candidates(mgr, min_elems: int):
+    out = []
+    for m in mgr.apa_modules.values():
+        W = m.weight_master
+        if W.requires_grad and W.is_cuda and W.dtype == torch.float32 and W.numel() >= min_elems and \
+                W.numel() % 4 == 0:
+            out.append(W)
+    return out
+
+
 class GradientAverager:
     def __init__(self, mgr, process_group=None, bucket_bytes: int = 64 << 20, reserved_sms: int = RESERVED_SMS,
-                 max_ctas: int = 0, block_bytes: int = 0, block_rows: int = 0):
+                 max_ctas: int = 0, block_bytes: int = 0, block_rows: int = 0, nvls: bool = True,
+                 nvls_min_elems: int = 1 << 20):
         self.world = dist.get_world_size(process_group)
         if max_ctas > 0 and dist.get_backend(process_group) == "nccl":
             process_group = _capped_nccl_group(process_group, max_ctas)
@@ -107,6 +201,22 @@ class GradientAverager:
                 seen.add(id(p))
         params = list(reversed(params))
         device = params[0].device if params else torch.device("cpu")
+        # large APALinear weight gradients through NVLink SHARP when the
+        # communicator is NCCL on GPUs with NVLink multicast; the rest (and
+        # everything when that is unavailable) in NCCL buckets
+        self.nvls = None
+        if nvls and device.type == "cuda" and dist.get_backend(process_group) == "nccl" and self.world > 1:
+            cands = [p for p in _nvls_candidates(mgr, nvls_min_elems) if id(p) in trainable]
+            if cands:
+                try:
+                    self.nvls = _NvlsGradients(cands, process_group, self.world,
+                                               dist.get_rank(process_group), device, max(1, reserved_sms))
+                except Exception as e:   # no symmetric memory / multicast here: NCCL for everything
+                    import warnings
+                    warnings.warn(f"NVLS gradient averaging unavailable ({e!r}); using NCCL buckets")
+                    self.nvls = None
+        if self.nvls is not None:
+            params = [p for p in params if id(p) not in self.nvls.index]
         self.bucket_bytes = bucket_bytes
         owner = {id(m.weight_master): m for m in mgr.apa_modules.values()}
         blocked = {}
@@ -147,8 +257,11 @@ class GradientAverager:
         for bi, b in enumerate(self.buckets):
             for p in b.params:
                 self.where[id(p)] = bi
-        # every averaged parameter, in bucket order (the ready mask's order)
+        # every averaged parameter, in bucket order, then the NVLS-averaged
+        # weights (the ready mask's order)
         self.order = [p for b in self.buckets for p in b.params]
+        if self.nvls is not None:
+            self.order += self.nvls.params
         pin = device.type == "cuda"
         self._mask_host = torch.zeros(max(1, len(self.order)), dtype=torch.int32, pin_memory=pin)
         self._ready = set()            # ids of parameters marked ready in this step
@@ -198,6 +311,11 @@ class GradientAverager:
             b.pending = len(b.params)
             b.handles = []
             b.blocks_issued = False
+        if self.nvls is not None:
+            for p in self.nvls.params:
+                v = self.nvls.views[id(p)]
+                if p.grad is None or p.grad.data_ptr() != v.data_ptr():
+                    p.grad = v
         self.next = 0
         self.ready_count = 0
         self.launch_marks = []
@@ -231,6 +349,21 @@ class GradientAverager:
         self._launch_ready()
 
     def _apa_ready(self, mod):
+        W = mod.weight_master
+        if self.nvls is not None and id(W) in self.nvls.index:
+            if self.armed and not self.accumulating:
+                if id(W) in self._ready:
+                    raise RuntimeError(
+                        "data parallel: a second backward pass produced gradients after their reduction started; "
+                        "run every backward pass of a step but the last inside APAManager.no_sync()")
+                self._ready.add(id(W))
+                if not self.limited:
+                    self._limit_gemms(True)
+                    self.limited = True
+                self.nvls.reduce(W)
+            if mod.bias_master is not None and mod.bias_master.requires_grad:
+                self._mark(mod.bias_master)
+            return
         self._mark(mod.weight_master)
         if mod.bias_master is not None and mod.bias_master.requires_grad:
             self._mark(mod.bias_master)
@@ -314,6 +447,8 @@ class GradientAverager:
     def grad_view(self, p):
         """p's view into its bucket while a step is armed (for a backward that
         finds p.grad cleared after pre_step), else None."""
+        if self.armed and self.nvls is not None and id(p) in self.nvls.index:
+            return self.nvls.views[id(p)]
         bi = self.where.get(id(p))
         if not self.armed or bi is None:
             return None
@@ -346,6 +481,8 @@ class GradientAverager:
         if self.capture_fork:
             stream.wait_stream(self.comm_stream)
             self.capture_fork = False
+        if self.nvls is not None:
+            self.nvls.join(stream)
 
     def _launch_ready(self):
         while self.next < len(self.buckets) and self.buckets[self.next].pending <= 0:
@@ -377,6 +514,18 @@ class GradientAverager:
         if self.graphed:
             return
         self.issue_remaining()
+        if self.nvls is not None:
+            dev = self.nvls.buf.device
+            for p in self.nvls.params:
+                if id(p) not in self._ready:
+                    # no gradient on this rank: it contributes zeros, and the
+                    # ranks still run the same reductions
+                    v = self.nvls.views[id(p)]
+                    v.zero_()
+                    if p.grad is None or p.grad.data_ptr() != v.data_ptr():
+                        p.grad = v
+                    self.nvls.reduce(p)
+            self.nvls.join(torch.cuda.current_stream(dev))
         for b in self.buckets:
             for h in b.handles:
                 h.wait()

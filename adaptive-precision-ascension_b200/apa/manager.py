@@ -94,7 +94,7 @@ class _LadderState:
 class APAManager:
     def __init__(self, model: nn.Module, config: APAConfig = APAConfig(), process_group=None,
                  sync_gradients: bool = True, bucket_bytes: int = 64 << 20, dp_reserved_sms: int = 16,
-                 dp_max_ctas: int = 0, dp_block_bytes: int = 0, dp_block_rows: int = 0):
+                 dp_max_ctas: int = 0, dp_block_bytes: int = 0, dp_block_rows: int = 0, dp_nvls: bool = True):
         self.model = model
         self.config = config
         self.step_count = 0
@@ -118,6 +118,7 @@ class APAManager:
         self._dp_max_ctas = dp_max_ctas           # >0: gradient communicator capped at this many CTAs
         self._dp_block_bytes = dp_block_bytes     # weights this large are reduced in row blocks (0: never)
         self._dp_block_rows = dp_block_rows       # rows per block (0: one GEMM wave)
+        self._dp_nvls = dp_nvls                   # large weight gradients averaged through NVLink SHARP
         self._dp = None
 
     # ------------------------------------------------------------------
@@ -301,6 +302,11 @@ class APAManager:
             before_wait()
             done.synchronize()
         rec = st.parse()
+        if rec["status"] & 0x100:
+            bits = _lib.device_status(clear=True)
+            raise _lib.APAKernelError(
+                f"a kernel's bounded wait gave up (device status 0x{bits:x}): a stalled pipeline, or in data "
+                "parallel runs a rank that did not reach the same reduction")
         if rec["status"] & 1:
             lv = [int(v) for v in rec["level"]]
             em = [float(v) for v in rec["ema"]]
@@ -456,7 +462,8 @@ class APAManager:
         from .dp import GradientAverager
         if self._dp is None:
             self._dp = GradientAverager(self, self._pg, self._bucket_bytes, self._dp_reserved_sms,
-                                        self._dp_max_ctas, self._dp_block_bytes, self._dp_block_rows)
+                                        self._dp_max_ctas, self._dp_block_bytes, self._dp_block_rows,
+                                        nvls=self._dp_nvls)
         return self._dp
 
     def _allreduce_grads(self):

@@ -8,3 +8,4 @@
 #include "noalloc.cu"
 #include "forensic.cu"
 #include "adamw.cu"
+#include "dp_nvls.cu"

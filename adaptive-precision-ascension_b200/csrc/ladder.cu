@@ -11,7 +11,9 @@
 // Decision record written to `out` (read by the host in one copy):
 //   int32  hdr[4]        {status bits, min_level, L, O}
 //                        status bit0: evaluation ran; bit1: batch has overflow
-//                        (skip); bit2: at least one module escalated
+//                        (skip); bit2: at least one module escalated; bit8:
+//                        the library status word is set (a bounded wait of
+//                        some earlier kernel gave up)
 //   int32  code[L]       bits 0-1 reason (1 OVERFLOW, 2 SILENT_UNDERFLOW),
 //                        bit 2 escalated, bits 4-5 level before
 //   int32  ocode[O]      1 when the non-APA leaf overflowed
@@ -216,7 +218,7 @@ __global__ void __launch_bounds__(256) ladder_eval_kernel(LadderArgs a) {
     }
   }
   if (tid == 0) {
-    hdr[0] = status;
+    hdr[0] = status | (g_status != 0u ? 0x100 : 0);
     hdr[1] = s_hdr[1];
     hdr[2] = L;
     hdr[3] = O;

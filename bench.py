@@ -166,6 +166,15 @@ def dist_info():
 # ---------------------------------------------------------------------------
 # our implementation
 # ---------------------------------------------------------------------------
+def grad_allreduce_desc(args):
+    if args.dp_nvls:
+        return ("APALinear weights of 1 Mi elements or more averaged through NVLink SHARP (multimem) where the GPUs "
+                "have it, the rest in NCCL buckets")
+    if args.dp_block_bytes > 0:
+        return f"NCCL, row blocks for weights >= {args.dp_block_bytes} B"
+    return "NCCL, whole buckets"
+
+
 def run_ours(args):
     sys.path.insert(0, PKG)
     import torch
@@ -204,7 +213,7 @@ def run_ours(args):
         lin = APALinear(K, N, config=cfg)
         lin.level = level
         mgr = APAManager(nn.Sequential(lin), cfg, bucket_bytes=args.dp_bucket_bytes,
-                         dp_block_bytes=args.dp_block_bytes)
+                         dp_block_bytes=args.dp_block_bytes, dp_nvls=bool(args.dp_nvls))
         return lin, mgr
 
     results = {}
@@ -281,11 +290,12 @@ def run_ours(args):
     vit = None
     if args.vit:
         vit = run_vit(torch, world, rank, dev, args.gpt_steps, max(4, args.warmup), barrier, max_over_ranks,
-                      graphed=not args.gpt_eager, dp_bucket_bytes=args.dp_bucket_bytes)
+                      graphed=not args.gpt_eager, dp_bucket_bytes=args.dp_bucket_bytes, dp_nvls=bool(args.dp_nvls))
     for name in args.gpt:
         gpt[name] = run_gpt(torch, dist, name, world, rank, dev, args.gpt_steps, max(4, args.warmup), barrier,
                             max_over_ranks, graphed=not args.gpt_eager, optimizer=args.gpt_optimizer,
-                            dp_block_bytes=args.dp_block_bytes, dp_bucket_bytes=args.dp_bucket_bytes)
+                            dp_block_bytes=args.dp_block_bytes, dp_bucket_bytes=args.dp_bucket_bytes,
+                            dp_nvls=bool(args.dp_nvls))
     out = None
     if rank == 0:
         fp8 = results["fp8"]
@@ -296,8 +306,7 @@ def run_ours(args):
             "data": "synthetic", "config": dict(CONFIG, parallelism=f"dp{world}",
                                                 launch="eager" if args.eager else
                                                 "cuda-graph replay of pre_step+fwd+bwd, ladder eager",
-                                                grad_allreduce=(f"row blocks for weights >= {args.dp_block_bytes} B"
-                                                                if args.dp_block_bytes > 0 else "whole buckets")),
+                                                grad_allreduce=grad_allreduce_desc(args)),
             "rungs": {k: {"tflops": round(v["tflops"], 2), "ms_per_step": round(v["ms_per_step"], 4),
                           "frac_of_peak": round(v["frac_of_peak"], 4),
                           "frac_of_library_gemm": round(v.get("frac_of_library_gemm", 0.0), 4)}
@@ -439,14 +448,14 @@ def gpt_batches(torch, cfgd, rank, device, n=4):
 
 
 def run_gpt(torch, dist, name, world, rank, dev, steps, warmup, barrier, max_over_ranks, graphed=True,
-            optimizer="torch", dp_block_bytes=0, dp_bucket_bytes=64 << 20):
+            optimizer="torch", dp_block_bytes=0, dp_bucket_bytes=64 << 20, dp_nvls=True):
     import torch.nn as nn
     import torch.nn.functional as F
     import apa
     from apa import APAManager
     cfgd = GPT_CONFIGS[name]
     model, cfg = build_gpt(torch, nn, F, apa, cfgd, dev)
-    mgr = APAManager(model, cfg, bucket_bytes=dp_bucket_bytes, dp_block_bytes=dp_block_bytes)
+    mgr = APAManager(model, cfg, bucket_bytes=dp_bucket_bytes, dp_block_bytes=dp_block_bytes, dp_nvls=dp_nvls)
     if optimizer == "apa":
         # AdamW with each APALinear weight's next working copy written in the same pass
         from apa.optim import APAAdamW
@@ -568,14 +577,15 @@ def build_vit(torch, nn, F, apa, cfgd, device):
     return ViT().to(device), cfg
 
 
-def run_vit(torch, world, rank, dev, steps, warmup, barrier, max_over_ranks, graphed=True, dp_bucket_bytes=64 << 20):
+def run_vit(torch, world, rank, dev, steps, warmup, barrier, max_over_ranks, graphed=True, dp_bucket_bytes=64 << 20,
+            dp_nvls=True):
     import torch.nn as nn
     import torch.nn.functional as F
     import apa
     from apa import APAManager
     cfgd = VIT_CONFIG
     model, cfg = build_vit(torch, nn, F, apa, cfgd, dev)
-    mgr = APAManager(model, cfg, bucket_bytes=dp_bucket_bytes)
+    mgr = APAManager(model, cfg, bucket_bytes=dp_bucket_bytes, dp_nvls=dp_nvls)
     opt = torch.optim.AdamW(mgr.get_trainable_parameters(), lr=cfgd["lr"], weight_decay=0.01, fused=True)
     g = torch.Generator().manual_seed(4321 + rank)
     B = cfgd["batch"]
@@ -1281,6 +1291,9 @@ def main():
                     help="data parallel: APALinear weights this large have their gradient computed and all-reduced "
                          "in row blocks (0, the default: one all-reduce per bucket after the whole gradient; "
                          "row blocks measured slower on 2 GPUs)")
+    ap.add_argument("--dp-nvls", type=int, default=1,
+                    help="data parallel: average large APALinear weight gradients through NVLink SHARP (1, the "
+                         "default, where the GPUs have NVLink multicast) or in NCCL buckets only (0)")
     ap.add_argument("--eager", action="store_true",
                     help="time the APALinear steps without CUDA-graph replay (every launch from the host)")
     ap.add_argument("--profile-case", default=None,

@@ -303,6 +303,33 @@ int apa_bias_grad_noalloc(const void* dy, int dy_dtype, int64_t rows, int64_t co
  * when `out_host` (pinned host memory) is given the record is also copied there
  * on the same stream, so the host needs one stream synchronisation.
  */
+/*
+ * Data-parallel averaging of a weight gradient through NVLink SHARP. The
+ * gradient (n fp32 elements, n % 4 == 0, 16-byte aligned) of every rank lives
+ * at the same offset of a symmetric allocation bound to an NVLink multicast
+ * object; mc_* arguments are multicast addresses of that allocation, *_local
+ * arguments this rank's own words of it (three u32 words per gradient:
+ * ready, done, epoch, all zero at start). Per gradient and step, in order:
+ *   apa_dp_signal on the stream that wrote the gradient (after the
+ *     weight-gradient GEMM): releases it and adds 1 to every rank's ready word;
+ *   apa_dp_allreduce (ctas CTAs, same ctas on every rank): waits until ready
+ *     reaches world x (epoch + 1), replaces this rank's 1/world shard of the
+ *     gradient on every rank by the mean over ranks (multimem.ld_reduce, x
+ *     1/world, multimem.st), adds 1 to every rank's done word;
+ *   apa_dp_wait after it on the same stream: waits until done reaches world x
+ *     ctas x (epoch + 1), then advances the epoch; work queued after it sees
+ *     the averaged gradient.
+ * Waits are bounded (2 s); on expiry the library status word is set (see
+ * apa_get_device_status; the ladder's decision record reports it) and the
+ * kernels return. Every rank must run the three for every such gradient in
+ * every step. No counterpart in the reference (it has no gradient
+ * collective; its only collective is the flag all-reduce, manager.py:186-187).
+ */
+int apa_dp_signal(unsigned int* mc_ready, void* stream);
+int apa_dp_allreduce(float* mc_grad, int64_t n, int world, int rank, const unsigned int* ready_local,
+                     unsigned int* mc_done, const unsigned int* epoch_local, int ctas, void* stream);
+int apa_dp_wait(const unsigned int* done_local, unsigned int* epoch_local, int world, int ctas, void* stream);
+
 int apa_ladder_pack(int L, const float* const* amax_ptr, const float* const* ratio_ptr,
                     const int32_t* const* flag_ptr, int O, const float* const* oamax_ptr,
                     const int32_t* const* oflag_ptr, int32_t* packed, void* stream);
