@@ -94,7 +94,7 @@ class _LadderState:
 class APAManager:
     def __init__(self, model: nn.Module, config: APAConfig = APAConfig(), process_group=None,
                  sync_gradients: bool = True, bucket_bytes: int = 64 << 20, dp_reserved_sms: int = 16,
-                 dp_max_ctas: int = 0, dp_block_bytes: int = 0, dp_block_rows: int = 0, dp_nvls: bool = True):
+                 dp_max_ctas: int = 0, dp_block_bytes: int = 0, dp_block_rows: int = 0, dp_nvls: bool = False):
         self.model = model
         self.config = config
         self.step_count = 0
@@ -118,7 +118,7 @@ class APAManager:
         self._dp_max_ctas = dp_max_ctas           # >0: gradient communicator capped at this many CTAs
         self._dp_block_bytes = dp_block_bytes     # weights this large are reduced in row blocks (0: never)
         self._dp_block_rows = dp_block_rows       # rows per block (0: one GEMM wave)
-        self._dp_nvls = dp_nvls                   # large weight gradients averaged through NVLink SHARP
+        self._dp_nvls = dp_nvls                   # opt-in: large weight gradients averaged through NVLink SHARP
         self._dp = None
 
     # ------------------------------------------------------------------

@@ -88,17 +88,32 @@ __global__ void __launch_bounds__(512) allreduce_kernel(float* mc_grad, int64_t 
   }
   __syncthreads();
   if (s_ok) {
+    // kIlp independent reductions in flight per thread: one multimem load
+    // crosses the switch and back, so a thread with a single outstanding load
+    // leaves the CTAs latency-bound far below the link rate
+    constexpr int kIlp = 8;
     const int64_t per = (n4 + world - 1) / world;
     const int64_t lo = (int64_t)rank * per;
     const int64_t hi = lo + per < n4 ? lo + per : n4;
-    for (int64_t i = lo + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < hi;
-         i += (int64_t)gridDim.x * blockDim.x) {
-      float4 v = mc_ld_reduce_f32x4(mc_grad + 4 * i);
-      v.x *= inv_world;
-      v.y *= inv_world;
-      v.z *= inv_world;
-      v.w *= inv_world;
-      mc_st_f32x4(mc_grad + 4 * i, v);
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t base = lo + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < hi; base += kIlp * stride) {
+      float4 v[kIlp];
+#pragma unroll
+      for (int u = 0; u < kIlp; ++u) {
+        const int64_t i = base + u * stride;
+        if (i < hi) v[u] = mc_ld_reduce_f32x4(mc_grad + 4 * i);
+      }
+#pragma unroll
+      for (int u = 0; u < kIlp; ++u) {
+        const int64_t i = base + u * stride;
+        if (i < hi) {
+          v[u].x *= inv_world;
+          v[u].y *= inv_world;
+          v[u].z *= inv_world;
+          v[u].w *= inv_world;
+          mc_st_f32x4(mc_grad + 4 * i, v[u]);
+        }
+      }
     }
   }
   __syncthreads();

@@ -1291,9 +1291,10 @@ def main():
                     help="data parallel: APALinear weights this large have their gradient computed and all-reduced "
                          "in row blocks (0, the default: one all-reduce per bucket after the whole gradient; "
                          "row blocks measured slower on 2 GPUs)")
-    ap.add_argument("--dp-nvls", type=int, default=1,
-                    help="data parallel: average large APALinear weight gradients through NVLink SHARP (1, the "
-                         "default, where the GPUs have NVLink multicast) or in NCCL buckets only (0)")
+    ap.add_argument("--dp-nvls", type=int, default=0,
+                    help="data parallel: average large APALinear weight gradients through NVLink SHARP with the "
+                         "library's own kernels (1, where the GPUs have NVLink multicast) or in NCCL buckets only "
+                         "(0, the default; the two measured level on two GPUs)")
     ap.add_argument("--eager", action="store_true",
                     help="time the APALinear steps without CUDA-graph replay (every launch from the host)")
     ap.add_argument("--profile-case", default=None,
