@@ -43,6 +43,7 @@ SIGNATURES = {
     "apa_linear_wgrad_ws": [_I, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _I64, _I, _VP, _VP, _VP, _I64, _VP],
     "apa_linear_wgrad_block": [_I, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _I64, _I, _VP, _VP, _I, _VP],
     "apa_set_gemm_sm_limit": [_I],
+    "apa_set_pdl": [_I],
     "apa_gemm_tn": [_I, _I, _VP, _I64, _VP, _I64, _VP, _I, _I64, _I64, _I64, _I64, _I, _I, _VP],
     "apa_gemm_plan": [_I, _I, _I64, _I64, _I64, _I, _I, _I, _VP, _VP],
     "apa_tensor_stats": [_VP, _I, _I64, _VP, _VP],

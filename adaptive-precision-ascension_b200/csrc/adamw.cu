@@ -80,6 +80,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
                       const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmT, AdamwArgs a) {
   using C = AwCfg<DST>;
   constexpr int S = kAStages;
+  pdl_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = su32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -104,6 +105,7 @@ __global__ void __launch_bounds__(kAThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  pdl_wait();   // the gradient and the optimizer state are final
 
   uint32_t mloc = 0;
   if (warp == kAConsumerWarps) {
@@ -324,7 +326,9 @@ int launch_adamw_cast_t(float* p, const float* g, float* m, float* v, int64_t ro
   a.has_dst_t = wq_t != nullptr;
   const int64_t tiles = ((rows + kAR - 1) / kAR) * ((cols + kAC - 1) / kAC);
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)num_sms() * blocks_per_sm));
-  adamw_cast_kernel<DST><<<(unsigned)grid, kAThreads, C::kSmemBytes, s>>>(mp, mg, mm, mv, md, mt, a);
+  if (launch_kernel(adamw_cast_kernel<DST>, dim3((unsigned)grid), dim3(kAThreads), C::kSmemBytes, s, 1, mp, mg, mm, mv,
+                    md, mt, a) != cudaSuccess)
+    return APA_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }
 

@@ -8,6 +8,7 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
@@ -34,6 +35,57 @@ __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
+}
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch. The library launches its kernels with
+// programmatic stream serialization, so the next kernel in a stream (or CUDA
+// graph) can be scheduled while the current one finishes: every kernel lets
+// its dependents launch as soon as all its CTAs are resident
+// (pdl_launch_dependents) and, after a prologue that touches only shared and
+// tensor memory and its parameters, waits in pdl_wait until the previous
+// kernel has completed and its memory operations are visible, before it reads
+// or writes global memory. Both instructions are no-ops for a launch without
+// the attribute. A dependent can only start on resources the running kernels
+// leave free, and only after every CTA of the kernel before it has started,
+// so the early start cannot starve that kernel.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// 1: launch with programmatic stream serialization (apa_set_pdl)
+static int g_pdl = 1;
+
+// cudaLaunchKernelEx with the library's launch attributes: programmatic
+// stream serialization when enabled, and a cluster of `cluster_x` CTAs
+// along x when cluster_x > 1.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                          int cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  unsigned int n = 0;
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (g_pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------------------

@@ -131,6 +131,8 @@ struct CastParams {
 
 template <int SRC, int DST>
 __global__ void __launch_bounds__(kThreads, 4) cast_kernel(CastParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   // 64 x 64 tile per iteration; thread t owns the 4 x 4 block at rows 4a..4a+3,
   // columns 4b..4b+3 (a = t / 16, b = t % 16). The transposed copy goes
   // through shared memory as packed column strips of 4 codes.
@@ -373,6 +375,8 @@ __global__ void __launch_bounds__(kThreads, 4) cast_kernel(CastParams p) {
 // tensors no fused kernel produced: non-APA module gradients, manual calls).
 template <int DT>
 __global__ void __launch_bounds__(256) amax_kernel(const void* src, int64_t n, float* amax, int* flag, int vec) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ uint32_t red[8];
   uint32_t mag = 0;
   constexpr int per = 16 / Elem<DT>::bytes;
@@ -416,6 +420,8 @@ template <int DT>
 __global__ void __launch_bounds__(256) underflow_kernel(const void* src, int64_t n, float vmin,
                                                         unsigned long long* counters, float* ratio_out,
                                                         int running_max) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ unsigned int s_nz[8], s_uf[8];
   const uint32_t vbits = __float_as_uint(vmin);
   unsigned int nz = 0, uf = 0;
@@ -463,6 +469,8 @@ constexpr int kColsumWarps = 32;
 __global__ void __launch_bounds__(kColsumWarps * 32) colsum_finalize_kernel(const float* partial, int64_t nparts,
                                                                            int64_t cols, int work_dt, float* out,
                                                                            int accumulate) {
+  pdl_launch_dependents();
+  pdl_wait();
   // block: 32 columns x 32 warps; warp w sums partial rows w, w+32, ... in
   // order (eight loads in flight), then warp 0 adds the 32 warp sums in order
   // (deterministic)
@@ -498,11 +506,14 @@ __global__ void __launch_bounds__(kColsumWarps * 32) colsum_finalize_kernel(cons
 void launch_colsum_finalize(const float* partial, int64_t nparts, int64_t cols, int work_dt, float* out,
                             int accumulate, cudaStream_t s) {
   const unsigned grid = (unsigned)((cols + 31) / 32);
-  colsum_finalize_kernel<<<grid, kColsumWarps * 32, 0, s>>>(partial, nparts, cols, work_dt, out, accumulate);
+  launch_kernel(colsum_finalize_kernel, dim3(grid), dim3(kColsumWarps * 32), 0, s, 1, partial, nparts, cols, work_dt,
+                out, accumulate);
 }
 
 // Zero a list of int32 words (per-step flag reset, manager.py:161-168).
 __global__ void zero_list_kernel(int* const* ptrs, int n) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) *ptrs[i] = 0;
 }
@@ -512,7 +523,8 @@ int launch_cast_t(CastParams& p, cudaStream_t s) {
   const int64_t tiles = ((p.rows + kTile - 1) / kTile) * ((p.cols + kTile - 1) / kTile);
   int64_t grid = std::min<int64_t>(tiles, (int64_t)num_sms() * 4);
   if (grid < 1) grid = 1;
-  cast_kernel<SRC, DST><<<(unsigned)grid, kThreads, 0, s>>>(p);
+  if (launch_kernel(cast_kernel<SRC, DST>, dim3((unsigned)grid), dim3(kThreads), 0, s, 1, p) != cudaSuccess)
+    return APA_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }
 
@@ -584,10 +596,10 @@ extern "C" int apa_amax(const void* src, int dtype, int64_t n, float* amax, int3
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   int* f = reinterpret_cast<int*>(flag);
   switch (dtype) {
-    case APA_DT_F32: amax_kernel<APA_DT_F32><<<grid, 256, 0, s>>>(src, n, amax, f, vec); break;
-    case APA_DT_F16: amax_kernel<APA_DT_F16><<<grid, 256, 0, s>>>(src, n, amax, f, vec); break;
-    case APA_DT_BF16: amax_kernel<APA_DT_BF16><<<grid, 256, 0, s>>>(src, n, amax, f, vec); break;
-    case APA_DT_E4M3: amax_kernel<APA_DT_E4M3><<<grid, 256, 0, s>>>(src, n, amax, f, vec); break;
+    case APA_DT_F32: apa::launch_kernel(amax_kernel<APA_DT_F32>, dim3(grid), dim3(256), 0, s, 1, src, n, amax, f, vec); break;
+    case APA_DT_F16: apa::launch_kernel(amax_kernel<APA_DT_F16>, dim3(grid), dim3(256), 0, s, 1, src, n, amax, f, vec); break;
+    case APA_DT_BF16: apa::launch_kernel(amax_kernel<APA_DT_BF16>, dim3(grid), dim3(256), 0, s, 1, src, n, amax, f, vec); break;
+    case APA_DT_E4M3: apa::launch_kernel(amax_kernel<APA_DT_E4M3>, dim3(grid), dim3(256), 0, s, 1, src, n, amax, f, vec); break;
     default: return APA_ERR_UNSUPPORTED;
   }
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
@@ -596,6 +608,8 @@ extern "C" int apa_amax(const void* src, int dtype, int64_t n, float* amax, int3
 namespace apa {
 namespace {
 __global__ void merge_kernel(float* amax, int* flag, const float* src) {
+  pdl_launch_dependents();
+  pdl_wait();
   telem_commit(amax, flag, mag_bits(*src));
 }
 }  // namespace
@@ -603,7 +617,8 @@ __global__ void merge_kernel(float* amax, int* flag, const float* src) {
 
 extern "C" int apa_merge_telemetry(float* amax, int32_t* flag, const float* src_amax, void* stream) {
   if (!src_amax) return APA_ERR_INVALID;
-  merge_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(amax, reinterpret_cast<int*>(flag), src_amax);
+  apa::launch_kernel(apa::merge_kernel, dim3(1), dim3(1), 0, static_cast<cudaStream_t>(stream), 1, amax,
+                     reinterpret_cast<int*>(flag), src_amax);
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }
 
@@ -613,10 +628,18 @@ extern "C" int apa_underflow_ratio(const void* src, int dtype, int64_t n, float 
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)num_sms() * 4));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case APA_DT_F32: underflow_kernel<APA_DT_F32><<<grid, 256, 0, s>>>(src, n, vmin, counters, ratio_out, running_max); break;
-    case APA_DT_F16: underflow_kernel<APA_DT_F16><<<grid, 256, 0, s>>>(src, n, vmin, counters, ratio_out, running_max); break;
-    case APA_DT_BF16: underflow_kernel<APA_DT_BF16><<<grid, 256, 0, s>>>(src, n, vmin, counters, ratio_out, running_max); break;
-    case APA_DT_E4M3: underflow_kernel<APA_DT_E4M3><<<grid, 256, 0, s>>>(src, n, vmin, counters, ratio_out, running_max); break;
+    case APA_DT_F32: apa::launch_kernel(underflow_kernel<APA_DT_F32>, dim3(grid), dim3(256), 0, s, 1, src, n, vmin, counters,
+                                          ratio_out, running_max);
+      break;
+    case APA_DT_F16: apa::launch_kernel(underflow_kernel<APA_DT_F16>, dim3(grid), dim3(256), 0, s, 1, src, n, vmin, counters,
+                                          ratio_out, running_max);
+      break;
+    case APA_DT_BF16: apa::launch_kernel(underflow_kernel<APA_DT_BF16>, dim3(grid), dim3(256), 0, s, 1, src, n, vmin, counters,
+                                          ratio_out, running_max);
+      break;
+    case APA_DT_E4M3: apa::launch_kernel(underflow_kernel<APA_DT_E4M3>, dim3(grid), dim3(256), 0, s, 1, src, n, vmin, counters,
+                                          ratio_out, running_max);
+      break;
     default: return APA_ERR_UNSUPPORTED;
   }
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
@@ -633,8 +656,8 @@ extern "C" int apa_colsum_finalize(const float* partial, int64_t nparts, int64_t
 extern "C" int apa_zero_list(int32_t* const* ptrs, int n, void* stream) {
   if (n < 0 || (n > 0 && !ptrs)) return APA_ERR_INVALID;
   if (n == 0) return APA_OK;
-  zero_list_kernel<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      reinterpret_cast<int* const*>(ptrs), n);
+  apa::launch_kernel(apa::zero_list_kernel, dim3((n + 255) / 256), dim3(256), 0, static_cast<cudaStream_t>(stream), 1,
+                     reinterpret_cast<int* const*>(ptrs), n);
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }
 

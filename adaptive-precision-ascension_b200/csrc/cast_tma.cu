@@ -149,6 +149,7 @@ __global__ void __launch_bounds__(kCastTmaThreads, DST == APA_DT_F32 ? 1 : 2)
                     const __grid_constant__ CUtensorMap tmT, TmaCastArgs p) {
   using C = TcCfg<SRC, DST>;
   constexpr int S = C::kStages;
+  pdl_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = su32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
@@ -174,6 +175,7 @@ __global__ void __launch_bounds__(kCastTmaThreads, DST == APA_DT_F32 ? 1 : 2)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  pdl_wait();   // the previous kernel's writes (the source, telemetry words) are visible
 
   uint32_t msrc = 0;
   if (warp == 4) {
@@ -540,7 +542,9 @@ int launch_cast_tma_t(const CastParams& cp, cudaStream_t s) {
   a.tf32 = cp.tf32;
   const int64_t tiles = ((cp.rows + kCTR - 1) / kCTR) * ((cp.cols + kCTC - 1) / kCTC);
   const int64_t grid = std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)num_sms() * blocks_per_sm));
-  cast_tma_kernel<SRC, DST><<<(unsigned)grid, kCastTmaThreads, C::kSmemBytes, s>>>(ms, md, mt, a);
+  if (launch_kernel(cast_tma_kernel<SRC, DST>, dim3((unsigned)grid), dim3(kCastTmaThreads), C::kSmemBytes, s, 1, ms,
+                    md, mt, a) != cudaSuccess)
+    return APA_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }
 

@@ -107,6 +107,7 @@ struct EpiArgs {
   int tma_out;                      // output written by TMA bulk-tensor stores
   int coalesced_out;                // output written by store_box_coalesced
   const void* bias;                 // FWD: working-dtype bias (nullable)
+  int bias_vec;                     // FWD: bias aligned for one vector load per 4 columns
   float* amax; int* flag;           // FWD: module telemetry; DGRAD: boundary_cast telemetry
   unsigned long long* counters;     // WGRAD: [nonzero, underflow, ticket], zero on entry
   float* ratio_max;                 // WGRAD: module gpu_underflow_ratio
@@ -353,13 +354,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 // ---------------------------------------------------------------------------
 // Epilogue helpers
 // ---------------------------------------------------------------------------
-template <int KIND>
-__device__ __forceinline__ float bias_value(const void* bias, int n) {
-  if constexpr (KIND == KIND_E4M3) return e4m3_to_f32(static_cast<const uint8_t*>(bias)[n]);
-  else if constexpr (KIND == KIND_F16) return f16_to_f32(static_cast<const uint16_t*>(bias)[n]);
-  else return static_cast<const float*>(bias)[n];
-}
-
 __device__ __forceinline__ void tmem_ld32_nowait(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -415,6 +409,102 @@ __device__ __forceinline__ uint32_t chunk_max(const uint32_t* r, int n, bool che
   return m;
 }
 
+// max(|a|, |b|, m), NaN-propagating: PTX max.NaN returns the canonical NaN
+// (bits 0x7FFFFFFF) when an operand is NaN, which orders above every
+// magnitude as the NaN's own bits do in the bit-pattern max of chunk_max;
+// for all other values the result is the same float.
+__device__ __forceinline__ float amax3(float a, float b, float m) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(fabsf(a)), "f"(fabsf(b)), "f"(m));
+  return r;
+}
+
+// chunk_max of a whole 64-value chunk (no masking): two independent chains
+// of three-input maxima.
+__device__ __forceinline__ uint32_t chunk_max_full(const uint32_t* r) {
+  float m0 = 0.0f, m1 = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 64; j += 4) {
+    m0 = amax3(fu(r[j]), fu(r[j + 1]), m0);
+    m1 = amax3(fu(r[j + 2]), fu(r[j + 3]), m1);
+  }
+  float m;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(m) : "f"(m0), "f"(m1));
+  return __float_as_uint(m);
+}
+
+// x0 += b0, x1 += b1 (fp32 words) in one packed instruction; add.rn.f32x2
+// rounds each lane exactly as add.rn.f32 does.
+__device__ __forceinline__ void add2(uint32_t& x0, uint32_t& x1, float b0, float b1) {
+  asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%0, %1};\n\tmov.b64 b, {%2, %3};\n\t"
+      "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "+r"(x0), "+r"(x1)
+      : "r"(__float_as_uint(b0)), "r"(__float_as_uint(b1)));
+}
+
+// The forward's bias for one epilogue warp's columns, in two halves: the raw
+// working-dtype words of 4 columns per lane (one vector load when aligned),
+// loaded one tile ahead so the load's latency hides behind the previous
+// tile's epilogue, then converted to fp32 into the warp's bias row in shared
+// memory. Columns past N read as +0.
+template <int WARP_COLS>
+struct BiasRaw {
+  static constexpr int kRounds = (WARP_COLS + 127) / 128;
+  uint32_t w[kRounds][4];
+};
+
+template <int KIND, int WARP_COLS>
+__device__ __forceinline__ void bias_load(const EpiArgs& ea, int col_base, int lane, BiasRaw<WARP_COLS>& br) {
+  constexpr int es = KindInfo<KIND>::bytes;
+#pragma unroll
+  for (int j = 0; j < BiasRaw<WARP_COLS>::kRounds; ++j) {
+    const int c = 128 * j + 4 * lane;
+    br.w[j][0] = br.w[j][1] = br.w[j][2] = br.w[j][3] = 0u;
+    if (c >= WARP_COLS) continue;
+    const int n = col_base + c;
+    const uint8_t* p = static_cast<const uint8_t*>(ea.bias) + (int64_t)n * es;
+    if (ea.bias_vec && n + 4 <= ea.N) {
+      if constexpr (es == 1) {
+        br.w[j][0] = *reinterpret_cast<const uint32_t*>(p);
+      } else if constexpr (es == 2) {
+        const uint2 v = *reinterpret_cast<const uint2*>(p);
+        br.w[j][0] = v.x; br.w[j][1] = v.y;
+      } else {
+        const uint4 v = *reinterpret_cast<const uint4*>(p);
+        br.w[j][0] = v.x; br.w[j][1] = v.y; br.w[j][2] = v.z; br.w[j][3] = v.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (n + e >= ea.N) break;
+        if constexpr (es == 1) br.w[j][0] |= (uint32_t)p[e] << (8 * e);
+        else if constexpr (es == 2) br.w[j][e >> 1] |= (uint32_t)reinterpret_cast<const uint16_t*>(p)[e] << (16 * (e & 1));
+        else br.w[j][e] = reinterpret_cast<const uint32_t*>(p)[e];
+      }
+    }
+  }
+}
+
+template <int KIND, int WARP_COLS>
+__device__ __forceinline__ void bias_store(float* sb, int lane, const BiasRaw<WARP_COLS>& br) {
+#pragma unroll
+  for (int j = 0; j < BiasRaw<WARP_COLS>::kRounds; ++j) {
+    const int c = 128 * j + 4 * lane;
+    if (c >= WARP_COLS) continue;
+    float4 f;
+    if constexpr (KIND == KIND_E4M3) {
+      f = make_float4(e4m3_to_f32(br.w[j][0] & 0xFFu), e4m3_to_f32((br.w[j][0] >> 8) & 0xFFu),
+                      e4m3_to_f32((br.w[j][0] >> 16) & 0xFFu), e4m3_to_f32(br.w[j][0] >> 24));
+    } else if constexpr (KIND == KIND_F16) {
+      f = make_float4(f16_to_f32((uint16_t)(br.w[j][0] & 0xFFFFu)), f16_to_f32((uint16_t)(br.w[j][0] >> 16)),
+                      f16_to_f32((uint16_t)(br.w[j][1] & 0xFFFFu)), f16_to_f32((uint16_t)(br.w[j][1] >> 16)));
+    } else {
+      f = make_float4(fu(br.w[j][0]), fu(br.w[j][1]), fu(br.w[j][2]), fu(br.w[j][3]));
+    }
+    *reinterpret_cast<float4*>(sb + c) = f;
+  }
+}
+
 // One 64-column unit of one row: r[0..63] hold the fp32 accumulators on
 // entry and the output words on exit (64 fp32 words, or 32 words of packed
 // 16-bit pairs). check: the tile is ragged, mask telemetry with row_ok / nv.
@@ -426,20 +516,19 @@ __device__ __forceinline__ void epi_unit(const EpiArgs& ea, const float* sb, uin
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
         const float4 b = reinterpret_cast<const float4*>(sb)[q];
-        r[4 * q + 0] = __float_as_uint(fu(r[4 * q + 0]) + b.x);
-        r[4 * q + 1] = __float_as_uint(fu(r[4 * q + 1]) + b.y);
-        r[4 * q + 2] = __float_as_uint(fu(r[4 * q + 2]) + b.z);
-        r[4 * q + 3] = __float_as_uint(fu(r[4 * q + 3]) + b.w);
+        add2(r[4 * q + 0], r[4 * q + 1], b.x, b.y);
+        add2(r[4 * q + 2], r[4 * q + 3], b.z, b.w);
       }
     }
-    if (ea.telem) st.mag = max(st.mag, chunk_max(r, 64, check, row_ok, nv));
+    if (ea.telem) st.mag = max(st.mag, check ? chunk_max(r, 64, check, row_ok, nv) : chunk_max_full(r));
     if constexpr (KIND == KIND_F16) {
 #pragma unroll
       for (int k = 0; k < 32; ++k) r[k] = f16x2_from_f32(fu(r[2 * k]), fu(r[2 * k + 1]));
     }
   } else if constexpr (EPI == EPI_DGRAD) {
     // the chunk max also selects the E4M3 conversion (NaN rule above 464)
-    const uint32_t m = (KIND == KIND_E4M3 || ea.telem) ? chunk_max(r, 64, check, row_ok, nv) : 0u;
+    const uint32_t m =
+        (KIND == KIND_E4M3 || ea.telem) ? (check ? chunk_max(r, 64, check, row_ok, nv) : chunk_max_full(r)) : 0u;
     if (ea.telem) st.mag = max(st.mag, m);
     const int od = ea.out_dt;
     if constexpr (KIND == KIND_E4M3) {
@@ -487,7 +576,7 @@ __device__ __forceinline__ void epi_unit(const EpiArgs& ea, const float* sb, uin
   } else {
     const uint32_t vb = __float_as_uint(ea.vmin);
     if constexpr (KIND == KIND_E4M3) {
-      const uint32_t m = chunk_max(r, 64, check, row_ok, nv);
+      const uint32_t m = check ? chunk_max(r, 64, check, row_ok, nv) : chunk_max_full(r);
       if (ea.telem) {
 #pragma unroll
         for (int j = 0; j < 64; ++j) {
@@ -652,6 +741,7 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
   constexpr int kEpiThreads = C::kEpiThreads;
   constexpr int kStages = C::kStages;
   constexpr int kElemPerSlab = kSlab / KindInfo<KIND>::bytes;
+  pdl_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
@@ -707,6 +797,8 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
   else __syncthreads();
   fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // the previous kernel's outputs (operands, counters, workspace) are ready
+  pdl_wait();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -798,6 +890,17 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
         else mbar_arrive(&tempty[acc]);
       }
     };
+    // forward bias: the first tile's columns now, each later tile's during
+    // the tile before it
+    BiasRaw<C::kWarpCols> braw;
+    auto bias_cols = [&](int w) {
+      int mb, nb;
+      tile_coords(unit_of(ea, w, kb_count).tile, num_m, num_n, kGroup, mb, nb);
+      return nb * BN + part * C::kWarpCols;
+    };
+    if constexpr (EPI == EPI_FWD) {
+      if (ea.bias != nullptr && unit0 < num_units) bias_load<KIND, C::kWarpCols>(ea, bias_cols(unit0), lane, braw);
+    }
     for (int w = unit0; w < num_units; w += units, ++local) {
       const Unit un = unit_of(ea, w, kb_count);
       const int tile = un.tile;
@@ -813,9 +916,10 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
       const bool check = (row0 + 32 > ea.M) || (col_base + C::kWarpCols > ea.N);
       if constexpr (EPI == EPI_FWD) {
         if (ea.bias != nullptr) {
-          for (int c = lane; c < C::kWarpCols; c += 32)
-            sb[c] = (col_base + c < ea.N) ? bias_value<KIND>(ea.bias, col_base + c) : 0.0f;
+          __syncwarp();   // every lane is done with the previous tile's row
+          bias_store<KIND, C::kWarpCols>(sb, lane, braw);
           __syncwarp();
+          if (w + units < num_units) bias_load<KIND, C::kWarpCols>(ea, bias_cols(w + units), lane, braw);
         }
       }
       // one lane waits and the warp follows its verdict, so a timeout can
@@ -1170,26 +1274,17 @@ int launch_t(const void* A, int64_t lda, const void* B, int64_t ldb, EpiArgs ea,
     if (int st = plan_tail(slots)) return st;
     int clusters = std::min(tiles, slots);
     clusters = std::max(1, clusters);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2 * clusters, 1, 1);
-    cfg.blockDim = dim3(C::kThreads, 1, 1);
-    cfg.dynamicSmemBytes = C::kSmemBytes;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    if (cudaLaunchKernelEx(&cfg, gemm_kernel<KIND, BN, EPI, true, EW>, ta, tb, to, ea) != cudaSuccess)
+    if (launch_kernel(gemm_kernel<KIND, BN, EPI, true, EW>, dim3(2 * clusters), dim3(C::kThreads), C::kSmemBytes,
+                      s, 2, ta, tb, to, ea) != cudaSuccess)
       return APA_ERR_CUDA;
   } else {
     const int slots = std::max(1, grid_cap > 0 ? grid_cap : num_sms());
     if (int st = plan_tail(slots)) return st;
     int grid = std::min(tiles, slots);
     if (grid < 1) grid = 1;
-    gemm_kernel<KIND, BN, EPI, false, EW><<<grid, C::kThreads, C::kSmemBytes, s>>>(ta, tb, to, ea);
+    if (launch_kernel(gemm_kernel<KIND, BN, EPI, false, EW>, dim3(grid), dim3(C::kThreads), C::kSmemBytes, s, 1,
+                      ta, tb, to, ea) != cudaSuccess)
+      return APA_ERR_CUDA;
   }
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }
@@ -1228,6 +1323,8 @@ __global__ void __launch_bounds__(256) wgrad_reduce_kernel(const float* ws, int 
   // 4, dw 16-byte aligned); rows * cols < 2^31 (the split path only takes
   // small gradients)
   constexpr int V = VEC ? 4 : 1;
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ unsigned int s_nz[8], s_uf[8];
   const uint32_t vb = __float_as_uint(vmin);
   unsigned int nz = 0, uf = 0;
@@ -1511,7 +1608,7 @@ int check_dims(int64_t M, int64_t N, int64_t K) {
 EpiArgs blank(int64_t M, int64_t N, int64_t K) {
   EpiArgs ea;
   ea.out = nullptr; ea.ldo = 0; ea.out_dt = APA_DT_F32; ea.vec_out = 0; ea.tma_out = 0; ea.coalesced_out = 0;
-  ea.bias = nullptr; ea.amax = nullptr; ea.flag = nullptr;
+  ea.bias = nullptr; ea.bias_vec = 0; ea.amax = nullptr; ea.flag = nullptr;
   ea.counters = nullptr; ea.ratio_max = nullptr; ea.vmin = 0.0f; ea.accumulate = 0; ea.finalize = 1; ea.telem = 0;
   ea.splits = 1; ea.kb_per_split = 0; ea.split_rows = 0;
   ea.sk_ws = nullptr; ea.sk_tickets = nullptr; ea.sk_ws_bytes = 0;
@@ -1536,6 +1633,8 @@ extern "C" int apa_linear_fwd(int rung, const void* xq, int64_t ldx, const void*
   ea.out_dt = rung == APA_RUNG_FP16 ? APA_DT_F16 : APA_DT_F32;
   ea.vec_out = out_vec(y, ldy, rung == APA_RUNG_FP16 ? 2 : 4);
   ea.bias = bias_q; ea.amax = amax; ea.flag = reinterpret_cast<int*>(flag);
+  const int bias_es = rung == APA_RUNG_FP8 ? 1 : rung == APA_RUNG_FP16 ? 2 : 4;
+  ea.bias_vec = (reinterpret_cast<uintptr_t>(bias_q) % (uintptr_t)(4 * bias_es)) == 0 ? 1 : 0;
   ea.telem = (amax || flag) ? 1 : 0;
   return apa::gemm_dispatch(rung, apa::gemm::EPI_FWD, xq, ldx, wq, ldw, ea, 0, 0, static_cast<cudaStream_t>(stream));
 }
@@ -1620,6 +1719,12 @@ extern "C" int apa_gemm_plan(int rung, int epilogue, int64_t M, int64_t N, int64
 extern "C" int apa_set_gemm_sm_limit(int limit) {
   if (limit < 0) return APA_ERR_INVALID;
   apa::g_gemm_sm_limit = limit;
+  return APA_OK;
+}
+
+extern "C" int apa_set_pdl(int enabled) {
+  if (enabled != 0 && enabled != 1) return APA_ERR_INVALID;
+  apa::g_pdl = enabled;
   return APA_OK;
 }
 
@@ -1720,13 +1825,10 @@ extern "C" int apa_linear_wgrad_ws(int rung, const void* dyqt, int64_t lddyt, co
   const float* ws = static_cast<const float*>(workspace);
   const int64_t slice = sp.rows_pad * sp.ld_ws;
   using namespace apa::gemm;
-#define APA_WGRAD_REDUCE(KIND_)                                                                                  \
-  if (vec)                                                                                                       \
-    wgrad_reduce_kernel<KIND_, true><<<grid, 256, 0, s>>>(ws, sp.splits, slice, sp.ld_ws, (int)N, (int)K, dw,    \
-                                                          lddw, accumulate, vmin, counters, ratio_max);          \
-  else                                                                                                           \
-    wgrad_reduce_kernel<KIND_, false><<<grid, 256, 0, s>>>(ws, sp.splits, slice, sp.ld_ws, (int)N, (int)K, dw,   \
-                                                           lddw, accumulate, vmin, counters, ratio_max);
+#define APA_WGRAD_REDUCE(KIND_)                                                                             \
+  apa::launch_kernel(vec ? wgrad_reduce_kernel<KIND_, true> : wgrad_reduce_kernel<KIND_, false>, dim3(grid),\
+                     dim3(256), 0, s, 1, ws, sp.splits, slice, sp.ld_ws, (int)N, (int)K, dw, lddw, accumulate,   \
+                     vmin, counters, ratio_max);
   switch (rung) {
     case APA_RUNG_FP8: APA_WGRAD_REDUCE(KIND_E4M3) break;
     case APA_RUNG_FP16: APA_WGRAD_REDUCE(KIND_F16) break;

@@ -45,6 +45,8 @@ __device__ __forceinline__ double thr_of(const LadderArgs& a, int lvl) {
 
 __global__ void ladder_pack_kernel(int L, const float* const* amax, const float* const* ratio, const int* const* flag,
                                    int O, const float* const* oamax, const int* const* oflag, int* packed) {
+  pdl_launch_dependents();
+  pdl_wait();
   // [hard][flag L][amax bits L][ratio bits L][oflag O][oamax bits O]; all
   // entries reduce correctly under an int32 MAX across ranks (non-negative
   // floats and NaN order like their bit patterns).
@@ -72,6 +74,8 @@ __global__ void ladder_pack_kernel(int L, const float* const* amax, const float*
 // Shared-memory image of the per-module state, filled by all threads so the
 // dependent global loads overlap; one thread then walks the modules in order.
 __global__ void __launch_bounds__(256) ladder_eval_kernel(LadderArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ double sh_d[];
   const int L = a.L, O = a.O;
   double* s_ema = sh_d;                                        // [L]
@@ -260,9 +264,9 @@ extern "C" int apa_ladder_pack(int L, const float* const* amax_ptr, const float*
   if (L < 0 || O < 0 || !packed) return APA_ERR_INVALID;
   if ((L > 0 && (!amax_ptr || !ratio_ptr || !flag_ptr)) || (O > 0 && (!oamax_ptr || !oflag_ptr)))
     return APA_ERR_INVALID;
-  ladder_pack_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      L, amax_ptr, ratio_ptr, reinterpret_cast<const int* const*>(flag_ptr), O, oamax_ptr,
-      reinterpret_cast<const int* const*>(oflag_ptr), reinterpret_cast<int*>(packed));
+  apa::launch_kernel(apa::ladder_pack_kernel, dim3(1), dim3(256), 0, static_cast<cudaStream_t>(stream), 1, L, amax_ptr,
+                     ratio_ptr, reinterpret_cast<const int* const*>(flag_ptr), O, oamax_ptr,
+                     reinterpret_cast<const int* const*>(oflag_ptr), reinterpret_cast<int*>(packed));
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }
 
@@ -294,7 +298,7 @@ extern "C" int apa_ladder_eval(int L, float* const* amax_ptr, float* const* rati
     if (cudaFuncSetAttribute(ladder_eval_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
       return APA_ERR_CUDA;
   }
-  ladder_eval_kernel<<<1, 256, smem, st>>>(a);
+  apa::launch_kernel(apa::ladder_eval_kernel, dim3(1), dim3(256), smem, st, 1, a);
   if (cudaGetLastError() != cudaSuccess) return APA_ERR_CUDA;
   if (out_host != nullptr &&
       cudaMemcpyAsync(out_host, out, ladder_record_bytes(L, O), cudaMemcpyDeviceToHost, st) != cudaSuccess)

@@ -188,6 +188,7 @@ def run_ours(args):
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    _lib.check(_lib.lib().apa_set_pdl(0 if args.no_pdl else 1), "apa_set_pdl")
 
     def barrier():
         if world > 1:
@@ -304,8 +305,10 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(fp8["ms_per_step"], 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3",
             "data": "synthetic", "config": dict(CONFIG, parallelism=f"dp{world}",
-                                                launch="eager" if args.eager else
-                                                "cuda-graph replay of pre_step+fwd+bwd, ladder eager",
+                                                launch=("eager" if args.eager else
+                                                        "cuda-graph replay of pre_step+fwd+bwd, ladder eager")
+                                                + ("" if args.no_pdl else
+                                                   ", programmatic dependent launch between the library's kernels"),
                                                 grad_allreduce=grad_allreduce_desc(args)),
             "rungs": {k: {"tflops": round(v["tflops"], 2), "ms_per_step": round(v["ms_per_step"], 4),
                           "frac_of_peak": round(v["frac_of_peak"], 4),
@@ -1069,6 +1072,118 @@ def run_reference(args):
             "cfg0": cfg0}
 
 
+def gemm_table():
+    """FP8 GEMMs of the GPT-2-medium layers (8192 tokens, d 1024, MLP 4096),
+    each timed back to back: a CUDA graph of 12 launches replayed, CUDA events
+    around one replay, the best of 5 (microseconds per launch, including the
+    2-4 us between consecutive kernels). Columns: the layer's fused entry
+    point (forward with bias and telemetry; input gradient with fp32 dx and
+    boundary-cast telemetry; weight gradient with counts and its split
+    workspace), the same GEMM bare (apa_gemm_tn, raw fp32 accumulator), and
+    cuBLASLt FP8 (torch._scaled_mm, unit scales, fp32 output) on the same
+    operands. One JSON line per GEMM."""
+    sys.path.insert(0, PKG)
+    import torch
+    from apa import _lib
+    lib = _lib.lib()
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    e4 = torch.float8_e4m3fn
+    T, NL = 8192, 12
+    one = torch.ones((), device=dev)
+
+    def per_launch(fn):
+        fn()
+        torch.cuda.synchronize()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(NL):
+                fn()
+        for _ in range(3):
+            graph.replay()
+        best = None
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / NL
+            best = us if best is None else min(best, us)
+        del graph
+        return round(best, 2)
+
+    amax = torch.zeros(1, device=dev)
+    flag = torch.zeros(1, dtype=torch.int32, device=dev)
+    layers = {"qkv": (3072, 1024), "proj": (1024, 1024), "fc": (4096, 1024), "fc2": (1024, 4096)}
+    for name, (nout, nin) in layers.items():
+        x = torch.randn(T, nin, device=dev, generator=g).to(e4)
+        w = (torch.randn(nout, nin, device=dev, generator=g) * 0.05).to(e4)
+        b = (torch.randn(nout, device=dev, generator=g) * 0.1).to(e4)
+        dy = torch.randn(T, nout, device=dev, generator=g).to(e4)
+        wt, dyt, xt = w.t().contiguous(), dy.t().contiguous(), x.t().contiguous()
+        for op in ("fwd", "dgrad", "wgrad"):
+            if op == "fwd":
+                A, B, m, n, k = x, w, T, nout, nin
+                out = torch.empty(m, n, device=dev)
+
+                def fused():
+                    _lib.check(lib.apa_linear_fwd(0, x.data_ptr(), nin, w.data_ptr(), nin, b.data_ptr(),
+                                                  out.data_ptr(), nout, T, nout, nin, amax.data_ptr(),
+                                                  flag.data_ptr(), _lib.stream_handle(dev)), "fwd")
+            elif op == "dgrad":
+                A, B, m, n, k = dy, wt, T, nin, nout
+                out = torch.empty(m, n, device=dev)
+
+                def fused():
+                    _lib.check(lib.apa_linear_dgrad(0, dy.data_ptr(), nout, wt.data_ptr(), nout, out.data_ptr(),
+                                                    _lib.DT_F32, nin, T, nout, nin, amax.data_ptr(), flag.data_ptr(),
+                                                    _lib.stream_handle(dev)), "dgrad")
+            else:
+                A, B, m, n, k = dyt, xt, nout, nin, T
+                out = torch.empty(m, n, device=dev)
+                cnt = torch.zeros(3, dtype=torch.int64, device=dev)
+                nb = ctypes.c_int64(0)
+                _lib.check(lib.apa_wgrad_workspace_bytes(0, T, nout, nin, ctypes.addressof(nb)), "ws")
+                ws = torch.empty(max(nb.value, 16), dtype=torch.uint8, device=dev)
+
+                def fused():
+                    if nb.value > 0:
+                        _lib.check(lib.apa_linear_wgrad_ws(0, dyt.data_ptr(), T, xt.data_ptr(), T, out.data_ptr(), nin,
+                                                           T, nout, nin, 0, cnt.data_ptr(), amax.data_ptr(),
+                                                           ws.data_ptr(), nb.value, _lib.stream_handle(dev)), "wgrad")
+                    else:
+                        _lib.check(lib.apa_linear_wgrad(0, dyt.data_ptr(), T, xt.data_ptr(), T, out.data_ptr(), nin,
+                                                        T, nout, nin, 0, cnt.data_ptr(), amax.data_ptr(),
+                                                        _lib.stream_handle(dev)), "wgrad")
+            raw = torch.empty(m, n, device=dev)
+
+            def bare():
+                _lib.check(lib.apa_gemm_tn(0, 3, A.data_ptr(), k, B.data_ptr(), k, raw.data_ptr(), _lib.DT_F32, n, m,
+                                           n, k, 0, 0, _lib.stream_handle(dev)), "gemm_tn")
+
+            def cublas():
+                torch._scaled_mm(A, B.t(), scale_a=one, scale_b=one, out_dtype=torch.float32)
+
+            tile, ew = ctypes.c_int(0), ctypes.c_int(0)
+            _lib.check(lib.apa_gemm_plan(0, {"fwd": 0, "dgrad": 1, "wgrad": 2}[op], m, n, k, _lib.DT_F32, 0, 0,
+                                         ctypes.addressof(tile), ctypes.addressof(ew)), "plan")
+            row = {"gemm": f"{name} {op}", "M": m, "N": n, "K": k, "plan": [tile.value, ew.value],
+                   "fused_us": per_launch(fused), "bare_us": per_launch(bare)}
+            try:
+                row["cublaslt_us"] = per_launch(cublas)
+            except RuntimeError as e:
+                row["cublaslt_us"] = None
+                row["cublaslt_error"] = str(e)[:120]
+            row["tflops_fused"] = round(2.0 * m * n * k / (row["fused_us"] * 1e-6) / 1e12, 1)
+            print(json.dumps(row), flush=True)
+
+
 def profile_case(case: str):
     """A few launches of one kernel at the bench shape, for ncu captures:
     gemm-fp8 / gemm-fp16 / gemm-tf32 (forward GEMM), dgrad-<rung> and
@@ -1085,16 +1200,17 @@ def profile_case(case: str):
     g = torch.Generator(device=dev).manual_seed(0)
     if case == "gemm-fp8-k1024":
         # an epilogue-bound FP8 forward: GPT-2-medium attention QKV projection
-        # (8192 tokens, 1024 -> 3072), fp32 output with telemetry
+        # (8192 tokens, 1024 -> 3072), fp32 output with bias and telemetry
         Mq, Kq, Nq = 8192, 1024, 3072
         x = torch.randn(Mq, Kq, device=dev, generator=g).to(torch.float8_e4m3fn)
         w = (torch.randn(Nq, Kq, device=dev, generator=g) * 0.02).to(torch.float8_e4m3fn)
+        b = (torch.randn(Nq, device=dev, generator=g) * 0.1).to(torch.float8_e4m3fn)
         y = torch.empty(Mq, Nq, device=dev)
         amax = torch.zeros(1, device=dev)
         flag = torch.zeros(1, dtype=torch.int32, device=dev)
         for _ in range(3):
-            _lib.check(lib.apa_linear_fwd(0, x.data_ptr(), Kq, w.data_ptr(), Kq, None, y.data_ptr(), Nq, Mq, Nq, Kq,
-                                          amax.data_ptr(), flag.data_ptr(), st), "fwd")
+            _lib.check(lib.apa_linear_fwd(0, x.data_ptr(), Kq, w.data_ptr(), Kq, b.data_ptr(), y.data_ptr(), Nq, Mq,
+                                          Nq, Kq, amax.data_ptr(), flag.data_ptr(), st), "fwd")
     elif case.startswith("gemm"):
         rung = {"gemm-fp8": 0, "gemm-fp16": 1, "gemm-tf32": 2}[case]
         dt = {0: torch.float8_e4m3fn, 1: torch.float16, 2: torch.float32}[rung]
@@ -1295,14 +1411,21 @@ def main():
                     help="data parallel: average large APALinear weight gradients through NVLink SHARP with the "
                          "library's own kernels (1, where the GPUs have NVLink multicast) or in NCCL buckets only "
                          "(0, the default; the two measured level on two GPUs)")
+    ap.add_argument("--no-pdl", action="store_true",
+                    help="launch the library's kernels in plain stream order instead of with programmatic dependent "
+                         "launch (each kernel's launch and prologue overlapping the end of the one before)")
     ap.add_argument("--eager", action="store_true",
                     help="time the APALinear steps without CUDA-graph replay (every launch from the host)")
     ap.add_argument("--profile-case", default=None,
                     help="run a few launches of one kernel for an ncu capture (gemm-fp8|gemm-fp16|gemm-tf32|gemm-fp8-k1024|"
+                         "gemm-table: timing table of the GPT-2-medium FP8 GEMMs against cuBLASLt|"
                          "dgrad-fp8|dgrad-fp16|dgrad-tf32|wgrad-fp8|wgrad-fp16|wgrad-tf32|cast|dyprep|cast-tf32|"
                          "dyprep-tf32|adamw-fp8), "
                          "or one profiled step (step-fp8|step-fp16|step-tf32|step-gpt2m|step-gpt-char|step-vit)")
     args = ap.parse_args()
+    if args.profile_case == "gemm-table":
+        gemm_table()
+        return
     if args.profile_case:
         profile_case(args.profile_case)
         return

@@ -207,6 +207,16 @@ int apa_linear_wgrad_ws(int rung, const void* dyqt, int64_t lddyt, const void* x
 int apa_set_gemm_sm_limit(int limit);
 
 /*
+ * Launch mode of every kernel of the library except the data-parallel NVLS
+ * ones: 1 (the default) = programmatic dependent launch, so a kernel's launch
+ * and prologue overlap the end of the kernel before it in the stream or CUDA
+ * graph (each kernel waits for that kernel's completion before it touches
+ * global memory); 0 = plain stream order. Affects launches made after the
+ * call. No counterpart in the reference.
+ */
+int apa_set_pdl(int enabled);
+
+/*
  * The same tcgen05 GEMM with a chosen epilogue and no telemetry side effects,
  * a chosen tile shape (APA_TILE_*; APA_TILE_AUTO picks one) and grid cap in
  * CTAs (0 = one CTA per SM). Used to time the bare GEMM against the fused
