@@ -44,15 +44,18 @@ SIGNATURES = {
     "apa_linear_wgrad_block": [_I, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _I64, _I, _VP, _VP, _I, _VP],
     "apa_set_gemm_sm_limit": [_I],
     "apa_set_pdl": [_I],
+    "apa_dp_regions": [_I64, _I64, _VP],
+    "apa_dp_region_signal": [_VP, _I64, _I64, _I64, _VP, _VP, _VP, _VP, _VP, _I, _I, _VP],
+    "apa_dp_region_reduce": [_VP, _I64, _I64, _I64, _VP, _VP, _VP, _VP, _VP, _I, _I, _I, _I, _VP],
+    "apa_dp_region_wait": [_VP, _VP, _I64, _VP],
+    "apa_linear_wgrad_dp": [_I, _VP, _I64, _VP, _I64, _VP, _I64, _I64, _I64, _I64, _VP, _VP, _VP, _I64, _VP,
+                            _VP, _VP, _VP, _VP, _VP, _I, _I, _VP],
     "apa_gemm_tn": [_I, _I, _VP, _I64, _VP, _I64, _VP, _I, _I64, _I64, _I64, _I64, _I, _I, _VP],
     "apa_gemm_plan": [_I, _I, _I64, _I64, _I64, _I, _I, _I, _VP, _VP],
     "apa_tensor_stats": [_VP, _I, _I64, _VP, _VP],
     "apa_adamw_cast": [_VP, _VP, _VP, _VP, _I64, _I64, _I64, _F, _F, _F, _F, _F, _I64, _VP, _I, _I64, _VP, _I64,
                        _VP, _VP],
     "apa_bias_grad_noalloc": [_VP, _I, _I64, _I64, _I64, _I, _VP, _I, _VP],
-    "apa_dp_signal": [_VP, _VP],
-    "apa_dp_allreduce": [_VP, _I64, _I, _I, _VP, _VP, _VP, _I, _VP],
-    "apa_dp_wait": [_VP, _VP, _I, _I, _VP],
     "apa_ladder_pack": [_I, _VP, _VP, _VP, _I, _VP, _VP, _VP, _VP],
     "apa_ladder_eval": [_I, _VP, _VP, _VP, _VP, _VP, _I, _VP, _VP, _VP, _I64, _I64,
                         ctypes.c_double, ctypes.c_double, _VP, _VP, _VP],

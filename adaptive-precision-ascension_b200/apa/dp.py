@@ -52,6 +52,7 @@ NVLS on NVSwitch systems, so the buckets stay the default.
 from __future__ import annotations
 
 import contextlib
+import ctypes
 from typing import Dict, List
 
 import torch
@@ -98,14 +99,23 @@ class _NvlsGradients:
     """APALinear weight gradients averaged through NVLink SHARP instead of
     NCCL: the fp32 gradients of the chosen weights live in one symmetric
     allocation bound to an NVLink multicast object (each weight's `.grad` is a
-    view into it, so the weight-gradient kernel writes there); after a
-    weight's gradient is written, apa_dp_signal releases it to every rank and,
-    on a side stream, apa_dp_allreduce averages this rank's 1/world shard of
-    it through the switch (multimem.ld_reduce, multimem.st back to every
-    rank) and apa_dp_wait holds the stream until every shard is in. Per GPU
-    and gradient of B bytes about 2 B / world cross NVLink, against
-    2 (world - 1) / world B for a ring all-reduce, and the reduction starts
-    as soon as that one gradient exists.
+    view into it, so the weight-gradient kernel writes there), cut into
+    regions of 32 rows x 64 columns, each averaged over the ranks by one
+    owner rank (multimem.ld_reduce through the switch, multimem.st of the
+    mean to every rank). The weight-gradient GEMM does it in its epilogue
+    (apa_linear_wgrad_dp: every region published as soon as it is stored,
+    the owned ones averaged while the tensor cores compute later tiles, and
+    any region whose contributions were not in within a few microseconds left
+    to apa_dp_region_reduce on a side stream); gradients written otherwise
+    take the standalone kernels (apa_dp_region_signal, then
+    apa_dp_region_reduce on the side stream). A one-thread apa_dp_region_wait
+    on the side stream marks the gradient complete; the step's later work
+    joins that stream. No kernel on the main stream waits long for another
+    rank, so ranks whose backward passes differ (a layer one rank skipped
+    gets its zeros at the end of that rank's backward) cannot block each
+    other. Per GPU and gradient
+    of B bytes about B crosses NVLink each way whatever the number of ranks,
+    against 2 (world - 1) / world B for a ring all-reduce.
 
     Every rank must reduce these gradients in every step: a rank whose layer
     produced no gradient contributes zeros (finish() launches its reduction);
@@ -114,20 +124,31 @@ class _NvlsGradients:
 
     def __init__(self, params, pg, world: int, rank: int, device, ctas: int):
         import torch.distributed._symmetric_memory as symm
+        from . import _lib
+        lib = _lib.lib()
         self.world, self.rank, self.ctas = world, rank, ctas
         self.index: Dict[int, int] = {}
         self.offset: Dict[int, int] = {}
+        self.regions: Dict[int, int] = {}
         off = 0
         for i, p in enumerate(params):
             self.index[id(p)] = i
             self.offset[id(p)] = off
             off += (p.numel() + 63) // 64 * 64          # 256-byte aligned gradients
-        self.ctr_off = off                              # per gradient: ready, done, epoch, pad (u32)
-        total = off + 4 * len(params)
+            n = ctypes.c_int64(0)
+            _lib.check(lib.apa_dp_regions(p.shape[0], p.shape[1], ctypes.addressof(n)), "apa_dp_regions")
+            self.regions[id(p)] = n.value
+        # counters (u32 words) per gradient: done, epoch, 2 spare, then one
+        # ready word per region and one deferred word per region, each run
+        # rounded up to 16 bytes
+        self.ctr: Dict[int, int] = {}
+        for p in params:
+            self.ctr[id(p)] = off
+            off += 4 + 2 * ((self.regions[id(p)] + 3) // 4 * 4)
         idx = device.index if device.index is not None else torch.cuda.current_device()
         if not symm._SymmetricMemory.has_multicast_support(symm.DeviceType.CUDA, idx):
             raise RuntimeError("no NVLink multicast support")
-        buf = symm.empty(total, dtype=torch.float32, device=device)
+        buf = symm.empty(off, dtype=torch.float32, device=device)
         group = pg if pg is not None else dist.group.WORLD
         hdl = symm.rendezvous(buf, group)
         if not int(hdl.multicast_ptr):
@@ -142,29 +163,75 @@ class _NvlsGradients:
         self.params = list(params)
         self.stream = None
         self.pending = False
+        self.fused_now = set()          # reduced by their weight-gradient GEMM this step
+        self.fused_calls = 0            # gradients reduced by their GEMM / by the standalone kernels
+        self.standalone_calls = 0
 
-    def _ctr(self, i: int, word: int, multicast: bool) -> int:
-        byte = (self.ctr_off + 4 * i + word) * 4
+    def _word(self, p, word: int, multicast: bool) -> int:
+        byte = (self.ctr[id(p)] + word) * 4
         return (self.mc if multicast else self.buf.data_ptr()) + byte
 
-    def reduce(self, p) -> None:
-        """Average p's gradient over the ranks (queued; see join)."""
-        from . import _lib
-        lib = _lib.lib()
-        i = self.index[id(p)]
+    def _counters(self, p):
+        """(ready local, ready multicast, done multicast, epoch local,
+        deferred local)."""
+        deferred = 4 + (self.regions[id(p)] + 3) // 4 * 4
+        return (self._word(p, 4, False), self._word(p, 4, True), self._word(p, 0, True), self._word(p, 1, False),
+                self._word(p, deferred, False))
+
+    def fused_args(self, p):
+        """The data-parallel arguments of apa_linear_wgrad_dp for p's
+        gradient (its view in this buffer): multicast address, counters,
+        world, rank. The caller launches the GEMM, then calls queued(p)."""
+        return (self.mc + self.offset[id(p)] * 4, *self._counters(p), self.world, self.rank)
+
+    def _side(self):
         dev = self.buf.device
-        cur = torch.cuda.current_stream(dev)
-        _lib.check(lib.apa_dp_signal(self._ctr(i, 0, True), _lib.stream_handle(dev)), "apa_dp_signal")
         if self.stream is None:
             self.stream = torch.cuda.Stream(device=dev)
-        self.stream.wait_stream(cur)
-        sh = self.stream.cuda_stream
-        _lib.check(lib.apa_dp_allreduce(self.mc + self.offset[id(p)] * 4, p.numel(), self.world, self.rank,
-                                        self._ctr(i, 0, False), self._ctr(i, 1, True), self._ctr(i, 2, False),
-                                        self.ctas, sh), "apa_dp_allreduce")
-        _lib.check(lib.apa_dp_wait(self._ctr(i, 1, False), self._ctr(i, 2, False), self.world, self.ctas, sh),
-                   "apa_dp_wait")
+        self.stream.wait_stream(torch.cuda.current_stream(dev))
+        return self.stream.cuda_stream
+
+    def _wait(self, p, sh) -> None:
+        from . import _lib
+        _lib.check(_lib.lib().apa_dp_region_wait(self._word(p, 0, False), self._word(p, 1, False),
+                                                 self.regions[id(p)], sh), "apa_dp_region_wait")
         self.pending = True
+
+    def queued(self, p) -> None:
+        """p's weight-gradient GEMM (apa_linear_wgrad_dp) is queued on the
+        current stream: the regions its epilogue deferred, then the
+        completion wait, go on the side stream."""
+        from . import _lib
+        self.fused_now.add(id(p))
+        self.fused_calls += 1
+        sh = self._side()
+        rows, cols = p.shape
+        _lib.check(_lib.lib().apa_dp_region_reduce(self.mc + self.offset[id(p)] * 4, cols, rows, cols,
+                                                   *self._counters(p), self.world, self.rank, 1, 4, sh),
+                   "apa_dp_region_reduce")
+        self._wait(p, sh)
+
+    def reduce(self, p) -> None:
+        """Average p's gradient over the ranks (queued; see join). A gradient
+        its GEMM already reduces needs nothing more."""
+        if id(p) in self.fused_now:
+            return
+        from . import _lib
+        lib = _lib.lib()
+        dev = self.buf.device
+        rows, cols = p.shape
+        ctr = self._counters(p)
+        mc = self.mc + self.offset[id(p)] * 4
+        _lib.check(lib.apa_dp_region_signal(mc, cols, rows, cols, *ctr, self.world, self.rank,
+                                            _lib.stream_handle(dev)), "apa_dp_region_signal")
+        sh = self._side()
+        _lib.check(lib.apa_dp_region_reduce(mc, cols, rows, cols, *ctr, self.world, self.rank, 0, self.ctas, sh),
+                   "apa_dp_region_reduce")
+        self.standalone_calls += 1
+        self._wait(p, sh)
+
+    def step_begin(self) -> None:
+        self.fused_now.clear()
 
     def join(self, stream) -> None:
         if self.pending:
@@ -177,7 +244,7 @@ def _nvls_candidates(mgr, min_elems: int):
     for m in mgr.apa_modules.values():
         W = m.weight_master
         if W.requires_grad and W.is_cuda and W.dtype == torch.float32 and W.numel() >= min_elems and \
-                W.numel() % 4 == 0:
+                W.dim() == 2 and W.shape[1] % 4 == 0:
             out.append(W)
     return out
 
@@ -269,6 +336,7 @@ class GradientAverager:
         pin = device.type == "cuda"
         self._mask_host = torch.zeros(max(1, len(self.order)), dtype=torch.int32, pin_memory=pin)
         self._ready = set()            # ids of parameters marked ready in this step
+        self._zeroed = set()
         self.accumulating = False      # inside no_sync(): gradients accumulate, nothing is reduced
         self.next = 0
         self.armed = False
@@ -316,6 +384,7 @@ class GradientAverager:
             b.handles = []
             b.blocks_issued = False
         if self.nvls is not None:
+            self.nvls.step_begin()
             for p in self.nvls.params:
                 v = self.nvls.views[id(p)]
                 if p.grad is None or p.grad.data_ptr() != v.data_ptr():
@@ -324,6 +393,7 @@ class GradientAverager:
         self.ready_count = 0
         self.launch_marks = []
         self._ready = set()
+        self._zeroed = set()           # NVLS gradients this rank contributed zeros for
         self.armed = True
 
     @contextlib.contextmanager
@@ -361,7 +431,8 @@ class GradientAverager:
                         "data parallel: a second backward pass produced gradients after their reduction started; "
                         "run every backward pass of a step but the last inside APAManager.no_sync()")
                 self._ready.add(id(W))
-                if not self.limited:
+                if id(W) not in self.nvls.fused_now and not self.limited:
+                    # the standalone reduction's CTAs need SMs beside the GEMMs
                     self._limit_gemms(True)
                     self.limited = True
                 self.nvls.reduce(W)
@@ -458,6 +529,18 @@ class GradientAverager:
             return None
         return self.buckets[bi].views[id(p)]
 
+    def nvls_fused(self, mod, g):
+        """The data-parallel arguments for computing mod's weight gradient
+        and averaging it over the ranks in one kernel (apa_linear_wgrad_dp),
+        or None: only for a gradient of the NVLS buffer, written into its own
+        view, while a step is armed and its reduction is due."""
+        W = mod.weight_master
+        if self.nvls is None or id(W) not in self.nvls.index or not self.armed or self.accumulating:
+            return None
+        if id(W) in self._ready or g.data_ptr() != self.nvls.views[id(W)].data_ptr():
+            return None
+        return self.nvls.fused_args(W)
+
     # row-block reduction of a large APALinear weight (called by its backward)
     def weight_blocks(self, mod, g):
         """The row blocks in which mod's weight gradient is to be computed this
@@ -503,9 +586,23 @@ class GradientAverager:
             self.limited = False
 
     def issue_remaining(self):
-        """Issue every bucket not yet issued, in order (asynchronous)."""
+        """Issue every bucket not yet issued, in order (asynchronous). NVLS
+        gradients this rank produced none of are contributed as zeros first:
+        the other ranks' weight-gradient GEMMs wait for this rank's regions,
+        so the contribution must be queued before any other collective of the
+        step (the telemetry all-reduce, the remaining buckets)."""
         if self.graphed:
             return
+        if self.nvls is not None:
+            dev = self.nvls.buf.device
+            for p in self.nvls.params:
+                if id(p) not in self._ready and id(p) not in self._zeroed:
+                    v = self.nvls.views[id(p)]
+                    v.zero_()
+                    if p.grad is None or p.grad.data_ptr() != v.data_ptr():
+                        p.grad = v
+                    self._zeroed.add(id(p))
+                    self.nvls.reduce(p)
         while self.next < len(self.buckets):
             self._launch(self.buckets[self.next])
             self.next += 1
@@ -519,17 +616,7 @@ class GradientAverager:
             return
         self.issue_remaining()
         if self.nvls is not None:
-            dev = self.nvls.buf.device
-            for p in self.nvls.params:
-                if id(p) not in self._ready:
-                    # no gradient on this rank: it contributes zeros, and the
-                    # ranks still run the same reductions
-                    v = self.nvls.views[id(p)]
-                    v.zero_()
-                    if p.grad is None or p.grad.data_ptr() != v.data_ptr():
-                        p.grad = v
-                    self.nvls.reduce(p)
-            self.nvls.join(torch.cuda.current_stream(dev))
+            self.nvls.join(torch.cuda.current_stream(self.nvls.buf.device))
         for b in self.buckets:
             for h in b.handles:
                 h.wait()

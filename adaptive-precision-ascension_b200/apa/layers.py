@@ -303,8 +303,19 @@ class _APALinearFn(torch.autograd.Function):
             nbytes = ctypes.c_int64(0)
             _lib.check(lib.apa_wgrad_workspace_bytes(level, M, N, K, ctypes.addressof(nbytes)),
                        "apa_wgrad_workspace_bytes")
-            blocks = dp.weight_blocks(mod, g) if (dp is not None and not accumulate) else None
-            if blocks:
+            fused = dp.nvls_fused(mod, g) if (dp is not None and not accumulate) else None
+            blocks = dp.weight_blocks(mod, g) if (dp is not None and not accumulate and fused is None) else None
+            if fused is not None:
+                # data parallel through NVLink SHARP: the GEMM's epilogue
+                # averages the gradient's regions over the ranks as it goes
+                ws = torch.empty(nbytes.value, dtype=torch.uint8, device=g.device) if nbytes.value > 0 else None
+                st = lib.apa_linear_wgrad_dp(level, dyqt.data_ptr(), dyqt.stride(0), ctx.xqt.data_ptr(),
+                                             ctx.xqt.stride(0), g.data_ptr(), K, M, N, K,
+                                             mod._uf_counters.data_ptr(), mod.gpu_underflow_ratio.data_ptr(),
+                                             _lib.ptr(ws), nbytes.value, *fused, s)
+                _lib.check(st, "apa_linear_wgrad_dp")
+                dp.nvls.queued(W)
+            elif blocks:
                 # data parallel: rows of the gradient in blocks, each block's
                 # all-reduce issued as soon as its rows are written
                 es = dyqt.element_size()

@@ -1,162 +1,109 @@
-// Data-parallel averaging of weight gradients through NVLink SHARP (NVLS):
-// every rank's fp32 gradient lives in one buffer of a symmetric allocation
-// bound to an NVLink multicast object; each rank averages its 1/world shard
-// of every gradient with multimem.ld_reduce (the switch sums the ranks'
-// copies) and writes the mean back to all ranks with one multimem.st.
+// Data-parallel averaging of weight gradients through NVLink SHARP (NVLS),
+// standalone form of the region protocol of dp_region.cuh, for gradients the
+// weight-gradient GEMM did not reduce in its epilogue (split-K plans, a rank
+// whose layer produced no gradient this step, accumulated gradients):
 //
-// Per gradient and step, three launches on the caller's streams:
-//   apa_dp_signal     1 thread, after the weight-gradient GEMM: release this
-//                     rank's gradient and add 1 to every rank's `ready` word
-//                     (one multimem.red through the switch).
-//   apa_dp_allreduce  a few CTAs: wait until `ready` reaches world x epoch
-//                     (every rank's gradient is complete), average this
-//                     rank's shard, then add 1 to every rank's `done` word.
-//   apa_dp_wait       1 thread: wait until `done` reaches world x ctas x
-//                     epoch (every shard of this gradient has been written on
-//                     this rank), then advance this rank's epoch.
-// Epochs are device words read and advanced by the kernels themselves, so the
-// launches can be replayed from a CUDA graph. No kernel waits on another
-// kernel of its own GPU: the signal and the local reduce precede the waits
-// that depend on them in stream order, and the waits depend only on the
-// other GPUs' kernels. Every wait is bounded (2 s of %globaltimer); on expiry
-// the kernel sets a bit in the library status word and returns.
+//   apa_dp_region_signal   after the gradient is written: publish every
+//                          region of this rank (one multimem.red each)
+//   apa_dp_region_reduce   a few CTAs: average the regions this rank owns
+//                          (waits for every rank's signal, ld_reduce, st),
+//                          or only those a GEMM epilogue deferred
+//   apa_dp_region_wait     one thread: wait until every region of the
+//                          gradient has been averaged, then advance the epoch
 //
-// Per GPU and gradient of B bytes the switch moves B / world in (the reduced
-// shard) and B / world out (the multicast store), against 2 (world-1)/world B
-// in and out for a ring all-reduce.
-#include "apa_common.cuh"
+// Per GPU and gradient of B bytes the switch moves about B in and B out
+// (the owned regions' sums and their multicast stores, and the reads other
+// owners make of this rank's memory), independent of the number of ranks.
+#include "dp_region.cuh"
 
 namespace apa {
 namespace dpnvls {
 
-constexpr unsigned int kStatusTimeoutReady = 1u << 12;
-constexpr unsigned int kStatusTimeoutDone = 1u << 13;
-
-__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void mc_red_add_release(unsigned int* mc, unsigned int v) {
-  asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(mc), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ float4 mc_ld_reduce_f32x4(const float* mc) {
-  float4 r;
-  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
-               : "l"(mc)
-               : "memory");
-  return r;
-}
-
-__device__ __forceinline__ void mc_st_f32x4(float* mc, float4 v) {
-  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc), "f"(v.x), "f"(v.y),
-               "f"(v.z), "f"(v.w)
-               : "memory");
-}
-
-// Wait (one thread) until *p >= target, at most kWaitLimitNs; false on expiry.
-__device__ __forceinline__ bool wait_at_least(const unsigned int* p, unsigned int target, unsigned int why) {
-  if ((int)(ld_acquire_sys(p) - target) >= 0) return true;
-  const unsigned long long t0 = global_ns();
-  while ((int)(ld_acquire_sys(p) - target) < 0) {
-    if (global_ns() - t0 > kWaitLimitNs) {
-      atomicOr(&g_status, why);
-      return false;
-    }
-  }
-  return true;
-}
-
-__global__ void signal_kernel(unsigned int* mc_ready) {
-  asm volatile("fence.acq_rel.sys;" ::: "memory");
-  mc_red_add_release(mc_ready, 1u);
-}
-
-// ready_local / epoch_local: this rank's words; mc_grad / mc_done: multicast
-// addresses. n4: float4 elements of the gradient; the shard of rank r is
-// float4s [r * per, min((r + 1) * per, n4)).
-__global__ void __launch_bounds__(512) allreduce_kernel(float* mc_grad, int64_t n4, int world, int rank,
-                                                        const unsigned int* ready_local, unsigned int* mc_done,
-                                                        const unsigned int* epoch_local, float inv_world) {
-  __shared__ int s_ok;
-  if (threadIdx.x == 0) {
-    const unsigned int target = (unsigned int)world * (*epoch_local + 1u);
-    s_ok = wait_at_least(ready_local, target, kStatusTimeoutReady) ? 1 : 0;
-  }
-  __syncthreads();
-  if (s_ok) {
-    // kIlp independent reductions in flight per thread: one multimem load
-    // crosses the switch and back, so a thread with a single outstanding load
-    // leaves the CTAs latency-bound far below the link rate
-    constexpr int kIlp = 8;
-    const int64_t per = (n4 + world - 1) / world;
-    const int64_t lo = (int64_t)rank * per;
-    const int64_t hi = lo + per < n4 ? lo + per : n4;
-    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t base = lo + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; base < hi; base += kIlp * stride) {
-      float4 v[kIlp];
-#pragma unroll
-      for (int u = 0; u < kIlp; ++u) {
-        const int64_t i = base + u * stride;
-        if (i < hi) v[u] = mc_ld_reduce_f32x4(mc_grad + 4 * i);
-      }
-#pragma unroll
-      for (int u = 0; u < kIlp; ++u) {
-        const int64_t i = base + u * stride;
-        if (i < hi) {
-          v[u].x *= inv_world;
-          v[u].y *= inv_world;
-          v[u].z *= inv_world;
-          v[u].w *= inv_world;
-          mc_st_f32x4(mc_grad + 4 * i, v[u]);
-        }
-      }
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    // every CTA signals, also after a timeout, so the other ranks' waits end
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-    mc_red_add_release(mc_done, 1u);
+// defer_owned: also hand this rank's own regions to the side stream's
+// pass over deferred regions (the caller runs no full reduce)
+__global__ void region_signal_kernel(dpr::RegionArgs a, int defer_owned) {
+  pdl_launch_dependents();
+  pdl_wait();
+  dpr::fence_sys();   // this rank's values (written by earlier kernels) before the signals
+  const unsigned int tag = defer_owned ? *a.epoch + 1u : 0u;
+  const int64_t n = dpr::num_regions(a.rows, a.cols);
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n; g += (int64_t)gridDim.x * blockDim.x) {
+    if (defer_owned && g % a.world == a.rank) a.deferred[g] = tag;
+    dpr::signal_ready(a, g);
   }
 }
 
-__global__ void wait_kernel(const unsigned int* done_local, unsigned int* epoch_local, int world, int ctas) {
-  const unsigned int e = *epoch_local + 1u;
-  wait_at_least(done_local, (unsigned int)world * (unsigned int)ctas * e, kStatusTimeoutDone);
-  *epoch_local = e;
+__global__ void __launch_bounds__(256) region_reduce_kernel(dpr::RegionArgs a, int only_deferred) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const unsigned int epoch = *a.epoch;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t n = dpr::num_regions(a.rows, a.cols);
+  const int ncb = dpr::region_cols(a.cols);
+  // owned regions rank, rank + world, ... in order, one warp each
+  for (int64_t g = a.rank + wid * a.world; g < n; g += warps * a.world) {
+    if (only_deferred && *(volatile unsigned int*)(a.deferred + g) != epoch + 1u) continue;   // warp-uniform
+    dpr::reduce_region(a, (int)(g / ncb), (int)(g % ncb), epoch, lane);
+  }
+}
+
+__global__ void region_wait_kernel(const unsigned int* done, unsigned int* epoch, unsigned int regions) {
+  const unsigned int e = *epoch + 1u;
+  dpr::wait_at_least(done, regions * e, dpr::kStatusTimeoutDone);
+  *epoch = e;
 }
 
 }  // namespace dpnvls
+
+int dp_region_signal(const dpr::RegionArgs& a, int defer_owned, cudaStream_t s) {
+  const int64_t n = dpr::num_regions(a.rows, a.cols);
+  const int grid = (int)std::min<int64_t>((n + 255) / 256, 64);
+  return launch_kernel(dpnvls::region_signal_kernel, dim3(grid), dim3(256), 0, s, 1, a, defer_owned) == cudaSuccess
+             ? APA_OK
+             : APA_ERR_CUDA;
+}
+
 }  // namespace apa
 
-namespace {
-bool dp_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-}  // namespace
-
-extern "C" int apa_dp_signal(unsigned int* mc_ready, void* stream) {
-  if (!mc_ready) return APA_ERR_INVALID;
-  apa::dpnvls::signal_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(mc_ready);
-  return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
+extern "C" int apa_dp_regions(int64_t rows, int64_t cols, int64_t* regions_out) {
+  if (!regions_out || rows <= 0 || cols <= 0 || rows >= (1ll << 31) || cols >= (1ll << 31)) return APA_ERR_INVALID;
+  *regions_out = apa::dpr::num_regions((int)rows, (int)cols);
+  return APA_OK;
 }
 
-extern "C" int apa_dp_allreduce(float* mc_grad, int64_t n, int world, int rank, const unsigned int* ready_local,
-                                unsigned int* mc_done, const unsigned int* epoch_local, int ctas, void* stream) {
-  if (!mc_grad || !ready_local || !mc_done || !epoch_local || n <= 0 || (n & 3) != 0 || world < 2 || world > 64 ||
-      rank < 0 || rank >= world || ctas < 1 || ctas > 1024)
-    return APA_ERR_INVALID;
-  if (!dp_aligned16(mc_grad)) return APA_ERR_ALIGN;
-  apa::dpnvls::allreduce_kernel<<<ctas, 512, 0, static_cast<cudaStream_t>(stream)>>>(
-      mc_grad, n / 4, world, rank, ready_local, mc_done, epoch_local, 1.0f / (float)world);
-  return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
+extern "C" int apa_dp_region_signal(float* grad_mc, int64_t ld, int64_t rows, int64_t cols,
+                                    const unsigned int* ready_local, unsigned int* ready_mc, unsigned int* done_mc,
+                                    const unsigned int* epoch_local, unsigned int* deferred_local, int world, int rank,
+                                    void* stream) {
+  apa::dpr::RegionArgs a;
+  if (int st = apa::dpr::make_region_args(&a, grad_mc, ld, rows, cols, ready_local, ready_mc, done_mc, epoch_local,
+                                          deferred_local, world, rank))
+    return st;
+  return apa::dp_region_signal(a, 0, static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int apa_dp_wait(const unsigned int* done_local, unsigned int* epoch_local, int world, int ctas,
-                           void* stream) {
-  if (!done_local || !epoch_local || world < 2 || ctas < 1) return APA_ERR_INVALID;
-  apa::dpnvls::wait_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(done_local, epoch_local, world, ctas);
+extern "C" int apa_dp_region_reduce(float* grad_mc, int64_t ld, int64_t rows, int64_t cols,
+                                    const unsigned int* ready_local, unsigned int* ready_mc, unsigned int* done_mc,
+                                    const unsigned int* epoch_local, unsigned int* deferred_local, int world, int rank,
+                                    int only_deferred, int ctas, void* stream) {
+  apa::dpr::RegionArgs a;
+  if (int st = apa::dpr::make_region_args(&a, grad_mc, ld, rows, cols, ready_local, ready_mc, done_mc, epoch_local,
+                                          deferred_local, world, rank))
+    return st;
+  if (ctas < 1 || ctas > 1024 || (only_deferred != 0 && only_deferred != 1)) return APA_ERR_INVALID;
+  return apa::launch_kernel(apa::dpnvls::region_reduce_kernel, dim3(ctas), dim3(256), 0,
+                            static_cast<cudaStream_t>(stream), 1, a, only_deferred) == cudaSuccess
+             ? APA_OK
+             : APA_ERR_CUDA;
+}
+
+extern "C" int apa_dp_region_wait(const unsigned int* done_local, unsigned int* epoch_local, int64_t regions,
+                                  void* stream) {
+  if (!done_local || !epoch_local || regions <= 0 || regions >= (1ll << 31)) return APA_ERR_INVALID;
+  // plain stream order: the wait depends on other GPUs only
+  apa::dpnvls::region_wait_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(done_local, epoch_local,
+                                                                                  (unsigned int)regions);
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
 }

@@ -51,6 +51,7 @@
 #include <cuda.h>
 #include <mutex>
 #include "apa_common.cuh"
+#include "dp_region.cuh"
 
 namespace apa {
 int num_sms();
@@ -127,6 +128,10 @@ struct EpiArgs {
   int* sk_tickets;                  // [tail tile][cta][epi warp], zero on entry and on exit
   int64_t sk_ws_bytes;              // caller workspace available (partials + tickets)
   int sk_first, sk_splits, sk_kb_per_split;
+  // WGRAD: the data-parallel average of the output run in the epilogue
+  // (dp.mc null: off): every warp publishes its 32 x 64 regions once they
+  // are stored and averages the ones this rank owns across the ranks
+  dpr::RegionArgs dp;
   int M, N, K;
 };
 
@@ -799,6 +804,8 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
   const uint32_t tmem_base = *tmem_slot;
   // the previous kernel's outputs (operands, counters, workspace) are ready
   pdl_wait();
+  // data parallel: this launch's place in the gradient's sequence of averages
+  const unsigned int dp_epoch = (EPI == EPI_WGRAD && ea.dp.mc != nullptr) ? *ea.dp.epoch : 0u;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -1036,6 +1043,35 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
         }
       }
       if (!released) release_acc(acc);   // this warp's columns lie past N: keep the count exact
+      if constexpr (EPI == EPI_WGRAD) {
+        if (ea.dp.mc != nullptr && row0 < ea.M) {
+          // data parallel: this warp's part of the tile is stored (TMA stores
+          // complete, direct stores fenced); publish its regions to every
+          // rank, then average the ones this rank owns while the tensor
+          // cores work on the next tiles
+          if (lane == 0 && inflight > 0) bulk_wait_all();
+          inflight = 0;
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          dpr::fence_sys();
+          __syncwarp();
+          const int rb = row0 / dpr::kRegionRows;
+          const int ncb = dpr::region_cols(ea.N);
+          if (lane == 0) {
+            for (int u = 0; u < kUnits; ++u) {
+              const int col0 = col_base + u * 64;
+              if (col0 >= ea.N) break;
+              dpr::signal_ready(ea.dp, (int64_t)rb * ncb + col0 / dpr::kRegionCols);
+            }
+          }
+          for (int u = 0; u < kUnits; ++u) {
+            const int col0 = col_base + u * 64;
+            if (col0 >= ea.N) break;
+            const int64_t g = (int64_t)rb * ncb + col0 / dpr::kRegionCols;
+            if ((int)(g % ea.dp.world) == ea.dp.rank)
+              dpr::reduce_region(ea.dp, rb, col0 / dpr::kRegionCols, dp_epoch, lane, /*defer=*/true);
+          }
+        }
+      }
     }
     const bool pending_store = inflight > 0;
     if (pending_store && lane == 0) bulk_wait_all();
@@ -1613,6 +1649,7 @@ EpiArgs blank(int64_t M, int64_t N, int64_t K) {
   ea.splits = 1; ea.kb_per_split = 0; ea.split_rows = 0;
   ea.sk_ws = nullptr; ea.sk_tickets = nullptr; ea.sk_ws_bytes = 0;
   ea.sk_first = 0; ea.sk_splits = 0; ea.sk_kb_per_split = 0;
+  ea.dp = apa::dpr::RegionArgs{};
   ea.M = (int)M; ea.N = (int)N; ea.K = (int)K;
   return ea;
 }
@@ -1661,8 +1698,9 @@ namespace {
 // aligned) lets the last partial wave of tiles be split along K (stream-K).
 int wgrad_gemm(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt, float* dw, int64_t lddw,
                int64_t M, int64_t N, int64_t K, int accumulate, unsigned long long* counters, float* ratio_max,
-               void* ws, int64_t ws_bytes, cudaStream_t s) {
+               void* ws, int64_t ws_bytes, cudaStream_t s, const apa::dpr::RegionArgs* dp = nullptr) {
   EpiArgs ea = blank(N, K, M);
+  if (dp != nullptr) ea.dp = *dp;
   ea.out = dw; ea.ldo = lddw; ea.out_dt = APA_DT_F32; ea.vec_out = out_vec(dw, lddw, 4);
   ea.accumulate = accumulate; ea.counters = counters; ea.ratio_max = ratio_max;
   ea.telem = counters ? 1 : 0;
@@ -1795,22 +1833,28 @@ extern "C" int apa_wgrad_workspace_bytes(int rung, int64_t M, int64_t N, int64_t
   return apa::tail_workspace_bytes(rung, apa::gemm::EPI_WGRAD, ea, bytes_out);
 }
 
-extern "C" int apa_linear_wgrad_ws(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt, float* dw,
-                                   int64_t lddw, int64_t M, int64_t N, int64_t K, int accumulate,
-                                   unsigned long long* counters, float* ratio_max, void* workspace,
-                                   int64_t workspace_bytes, void* stream) {
-  if (int st = check_dims(N, K, M)) return st;
-  if (!dyqt || !xqt || !dw || lddw < K || lddyt < M || ldxt < M) return APA_ERR_INVALID;
-  if (rung != APA_RUNG_TF32 && !counters) return APA_ERR_INVALID;
-  const apa::SplitPlan sp = apa::plan_wgrad_split(rung, N, K, M);
+namespace apa {
+// dp_nvls.cu: publish every region of a gradient (defer_owned: and hand this
+// rank's own to the deferred pass)
+int dp_region_signal(const dpr::RegionArgs& a, int defer_owned, cudaStream_t s);
+}  // namespace apa
+
+namespace {
+
+// Whether this weight gradient is computed split along the tokens (two
+// kernels: fp32 partials into the workspace, then their ordered sum with the
+// weight-gradient epilogue) and the workspace is enough for it.
+bool wgrad_is_split(const apa::SplitPlan& sp, int64_t N, int64_t K, const void* workspace, int64_t workspace_bytes) {
   const int64_t need = sp.splits > 1 ? (int64_t)sp.splits * sp.rows_pad * sp.ld_ws * 4 : 0;
   // the reduction kernel takes at most 8 splits and 32-bit element indices
   // (the plan only splits outputs of a few tiles, so neither limit is reached)
-  if (need == 0 || !workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15u) ||
-      N * K >= (1ll << 31) || sp.splits > 8)
-    return wgrad_gemm(rung, dyqt, lddyt, xqt, ldxt, dw, lddw, M, N, K, accumulate, counters, ratio_max, workspace,
-                      workspace_bytes, static_cast<cudaStream_t>(stream));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return !(need == 0 || !workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 15u) ||
+           N * K >= (1ll << 31) || sp.splits > 8);
+}
+
+int wgrad_split(const apa::SplitPlan& sp, int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt,
+                float* dw, int64_t lddw, int64_t M, int64_t N, int64_t K, int accumulate,
+                unsigned long long* counters, float* ratio_max, void* workspace, cudaStream_t s) {
   // phase 1: raw fp32 partial sums, one slice per split
   EpiArgs ea = blank(N, K, M);
   ea.out = workspace; ea.ldo = sp.ld_ws; ea.out_dt = APA_DT_F32; ea.vec_out = 1;
@@ -1836,4 +1880,48 @@ extern "C" int apa_linear_wgrad_ws(int rung, const void* dyqt, int64_t lddyt, co
   }
 #undef APA_WGRAD_REDUCE
   return cudaGetLastError() == cudaSuccess ? APA_OK : APA_ERR_CUDA;
+}
+
+}  // namespace
+
+extern "C" int apa_linear_wgrad_ws(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt, float* dw,
+                                   int64_t lddw, int64_t M, int64_t N, int64_t K, int accumulate,
+                                   unsigned long long* counters, float* ratio_max, void* workspace,
+                                   int64_t workspace_bytes, void* stream) {
+  if (int st = check_dims(N, K, M)) return st;
+  if (!dyqt || !xqt || !dw || lddw < K || lddyt < M || ldxt < M) return APA_ERR_INVALID;
+  if (rung != APA_RUNG_TF32 && !counters) return APA_ERR_INVALID;
+  const apa::SplitPlan sp = apa::plan_wgrad_split(rung, N, K, M);
+  if (!wgrad_is_split(sp, N, K, workspace, workspace_bytes))
+    return wgrad_gemm(rung, dyqt, lddyt, xqt, ldxt, dw, lddw, M, N, K, accumulate, counters, ratio_max, workspace,
+                      workspace_bytes, static_cast<cudaStream_t>(stream));
+  return wgrad_split(sp, rung, dyqt, lddyt, xqt, ldxt, dw, lddw, M, N, K, accumulate, counters, ratio_max, workspace,
+                     static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int apa_linear_wgrad_dp(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt,
+                                   float* dw, int64_t lddw, int64_t M, int64_t N, int64_t K,
+                                   unsigned long long* counters, float* ratio_max, void* workspace,
+                                   int64_t workspace_bytes, float* dw_mc, const unsigned int* ready_local,
+                                   unsigned int* ready_mc, unsigned int* done_mc, const unsigned int* epoch_local,
+                                   unsigned int* deferred_local, int world, int rank, void* stream) {
+  if (int st = check_dims(N, K, M)) return st;
+  if (!dyqt || !xqt || !dw || lddw < K || lddyt < M || ldxt < M) return APA_ERR_INVALID;
+  if (rung != APA_RUNG_TF32 && !counters) return APA_ERR_INVALID;
+  apa::dpr::RegionArgs dp;
+  if (int st = apa::dpr::make_region_args(&dp, dw_mc, lddw, N, K, ready_local, ready_mc, done_mc, epoch_local,
+                                          deferred_local, world, rank))
+    return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const apa::SplitPlan sp = apa::plan_wgrad_split(rung, N, K, M);
+  if (!wgrad_is_split(sp, N, K, workspace, workspace_bytes))
+    return wgrad_gemm(rung, dyqt, lddyt, xqt, ldxt, dw, lddw, M, N, K, 0, counters, ratio_max, workspace,
+                      workspace_bytes, s, &dp);
+  // split along the tokens: the gradient is complete after the second
+  // kernel, then the standalone form of the same regions
+  if (int st = wgrad_split(sp, rung, dyqt, lddyt, xqt, ldxt, dw, lddw, M, N, K, 0, counters, ratio_max, workspace, s))
+    return st;
+  // kernel, then its regions published with this rank's own marked deferred
+  // (the caller's side-stream pass averages them; nothing waits here)
+  return apa::dp_region_signal(dp, 1, s);
 }

@@ -314,31 +314,64 @@ int apa_bias_grad_noalloc(const void* dy, int dy_dtype, int64_t rows, int64_t co
  * on the same stream, so the host needs one stream synchronisation.
  */
 /*
- * Data-parallel averaging of a weight gradient through NVLink SHARP. The
- * gradient (n fp32 elements, n % 4 == 0, 16-byte aligned) of every rank lives
- * at the same offset of a symmetric allocation bound to an NVLink multicast
- * object; mc_* arguments are multicast addresses of that allocation, *_local
- * arguments this rank's own words of it (three u32 words per gradient:
- * ready, done, epoch, all zero at start). Per gradient and step, in order:
- *   apa_dp_signal on the stream that wrote the gradient (after the
- *     weight-gradient GEMM): releases it and adds 1 to every rank's ready word;
- *   apa_dp_allreduce (ctas CTAs, same ctas on every rank): waits until ready
- *     reaches world x (epoch + 1), replaces this rank's 1/world shard of the
- *     gradient on every rank by the mean over ranks (multimem.ld_reduce, x
- *     1/world, multimem.st), adds 1 to every rank's done word;
- *   apa_dp_wait after it on the same stream: waits until done reaches world x
- *     ctas x (epoch + 1), then advances the epoch; work queued after it sees
- *     the averaged gradient.
- * Waits are bounded (2 s); on expiry the library status word is set (see
- * apa_get_device_status; the ladder's decision record reports it) and the
- * kernels return. Every rank must run the three for every such gradient in
- * every step. No counterpart in the reference (it has no gradient
- * collective; its only collective is the flag all-reduce, manager.py:186-187).
+ * Data-parallel averaging of an fp32 weight gradient [rows, cols] (row pitch
+ * ld; cols and ld multiples of 4, 16-byte aligned) through NVLink SHARP. The
+ * gradient of every rank lives at the same offset of a symmetric allocation
+ * bound to an NVLink multicast object; grad_mc and *_mc are multicast
+ * addresses in it, *_local this rank's own words (u32, zero at start): one
+ * ready counter and one deferred word per region (apa_dp_regions: regions of
+ * 32 rows x 64 columns, region g averaged by rank g % world), one done
+ * counter and one epoch word per gradient. Per gradient and step, on every
+ * rank:
+ *   either apa_linear_wgrad_dp (the GEMM runs the protocol in its epilogue)
+ *     and, on a side stream after it, apa_dp_region_reduce with
+ *     only_deferred = 1 (the regions the epilogue did not find ready within
+ *     a few microseconds),
+ *   or, after the gradient is written some other way, apa_dp_region_signal on
+ *     the stream that wrote it and apa_dp_region_reduce (only_deferred = 0)
+ *     after it;
+ *   then apa_dp_region_wait: waits until every region is averaged (done
+ *     reaches regions x (epoch + 1)), then advances the epoch; work queued
+ *     after it sees the mean over ranks in every rank's gradient.
+ * Only apa_dp_region_reduce and apa_dp_region_wait wait long for other ranks,
+ * so a rank's main stream never does. Those waits are bounded (2 s); on
+ * expiry the library status word is set (see apa_get_device_status; the
+ * ladder's decision record reports it), the waiter still signals, later
+ * waits give up at once, and the kernels return. Ranks may mix the two forms.
+ * No counterpart in the reference (it has no gradient collective; its only
+ * collective is the flag all-reduce, manager.py:186-187).
  */
-int apa_dp_signal(unsigned int* mc_ready, void* stream);
-int apa_dp_allreduce(float* mc_grad, int64_t n, int world, int rank, const unsigned int* ready_local,
-                     unsigned int* mc_done, const unsigned int* epoch_local, int ctas, void* stream);
-int apa_dp_wait(const unsigned int* done_local, unsigned int* epoch_local, int world, int ctas, void* stream);
+int apa_dp_regions(int64_t rows, int64_t cols, int64_t* regions_out);
+int apa_dp_region_signal(float* grad_mc, int64_t ld, int64_t rows, int64_t cols, const unsigned int* ready_local,
+                         unsigned int* ready_mc, unsigned int* done_mc, const unsigned int* epoch_local,
+                         unsigned int* deferred_local, int world, int rank, void* stream);
+int apa_dp_region_reduce(float* grad_mc, int64_t ld, int64_t rows, int64_t cols, const unsigned int* ready_local,
+                         unsigned int* ready_mc, unsigned int* done_mc, const unsigned int* epoch_local,
+                         unsigned int* deferred_local, int world, int rank, int only_deferred, int ctas,
+                         void* stream);
+int apa_dp_region_wait(const unsigned int* done_local, unsigned int* epoch_local, int64_t regions, void* stream);
+
+/*
+ * Weight gradient and its data-parallel average in one kernel: dw = this
+ * rank's gradient exactly as apa_linear_wgrad_ws computes it (accumulate = 0;
+ * counters and ratio_max of this rank's gradient), then every 32 x 64 region
+ * of it, as soon as this rank's values are stored, published to the other
+ * ranks, and the regions this rank owns averaged through the switch by the
+ * same epilogue warps while the tensor cores compute later tiles (a region
+ * whose contributions are not all in within a few microseconds is deferred
+ * to the side stream's apa_dp_region_reduce pass). dw_mc is the multicast
+ * address of dw; the counters as for apa_dp_region_*. Work that reads dw
+ * queues after apa_dp_region_wait. Shapes whose weight gradient is split
+ * along the tokens take the split kernels, then publish every region and
+ * defer this rank's own, inside this call. Replaces the same step as
+ * apa_linear_wgrad_ws followed by the gradient all-reduce.
+ */
+int apa_linear_wgrad_dp(int rung, const void* dyqt, int64_t lddyt, const void* xqt, int64_t ldxt, float* dw,
+                        int64_t lddw, int64_t M, int64_t N, int64_t K, unsigned long long* counters,
+                        float* ratio_max, void* workspace, int64_t workspace_bytes, float* dw_mc,
+                        const unsigned int* ready_local, unsigned int* ready_mc, unsigned int* done_mc,
+                        const unsigned int* epoch_local, unsigned int* deferred_local, int world, int rank,
+                        void* stream);
 
 int apa_ladder_pack(int L, const float* const* amax_ptr, const float* const* ratio_ptr,
                     const int32_t* const* flag_ptr, int O, const float* const* oamax_ptr,

@@ -1,16 +1,32 @@
-"""Data-parallel weight gradients averaged through NVLink SHARP (the
-apa_dp_signal / apa_dp_allreduce / apa_dp_wait kernels over a symmetric,
-multicast-bound buffer) against the NCCL bucket path, on 2 GPUs (skipped
-with fewer, or where the GPUs have no NVLink multicast).
+"""Data-parallel weight gradients averaged through NVLink SHARP (the region
+protocol: apa_linear_wgrad_dp, whose epilogue publishes every 32 x 64 region
+of the gradient as it is stored and averages the regions its rank owns with
+multimem.ld_reduce / multimem.st, and the standalone apa_dp_region_signal /
+apa_dp_region_reduce for gradients written otherwise) against the NCCL bucket
+path, on 2 GPUs (skipped with fewer, or where the GPUs have no NVLink
+multicast).
 
-Each rank trains the same model (a 2048 x 2048 APALinear, large enough for
-the NVLS path, then a small one) on its own batches for a few AdamW steps,
-once with the NVLS path and once with NCCL buckets only. At the FP8 rung the
-per-rank gradients are E4M3 values, whose sums over a few ranks are exact in
-fp32, so both paths average to the same bits and the weights after training
-are identical; at FP16 and TF32 the two reductions add in different orders,
-so the weights agree to fp32 rounding. In every case the ranks' replicas
-are bit-identical to each other. Eager and graph-replayed steps."""
+Each rank trains the same model on its own batches for a few AdamW steps,
+once with the NVLS path and once with NCCL buckets only:
+
+* fused: a 2048 x 2048 APALinear (large enough for the NVLS path; its weight
+  gradient is one GEMM, so the GEMM's epilogue runs the reduction), then a
+  small one;
+* split: a 1024 x 1024 APALinear over 8192 tokens, whose weight gradient is
+  split along the tokens (two kernels), so the standalone kernels reduce it
+  inside apa_linear_wgrad_dp;
+* unused: rank 1 skips the middle 2048 x 2048 layer, so rank 0's GEMM
+  epilogue and rank 1's standalone reduction of zeros take part in the same
+  averages (eager only: a captured step issues the reductions of the
+  gradients its capture produced, so the ranks' graphs must take the same
+  layers).
+
+At the FP8 rung the per-rank gradients are E4M3 values, whose sums over a few
+ranks are exact in fp32, so both paths average to the same bits and the
+weights after training are identical; at FP16 and TF32 the two reductions add
+in different orders, so the weights agree to fp32 rounding. In every case the
+ranks' replicas are bit-identical to each other. Eager and graph-replayed
+steps."""
 import os
 import socket
 
@@ -30,13 +46,33 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q, level, graphed):
+def _model(case, cfg, dev, rank):
+    import torch.nn as nn
+    from apa import APALinear
+
+    class Net(nn.Module):
+        def __init__(self):
+            super().__init__()
+            d = 1024 if case == "split" else 2048
+            self.a = APALinear(d, d, config=cfg)
+            self.b = APALinear(d, d, config=cfg) if case == "unused" else None
+            self.head = APALinear(d, 16, config=cfg)
+
+        def forward(self, x):
+            h = torch.relu(self.a(x))
+            if self.b is not None and rank == 0:
+                h = torch.relu(self.b(h))
+            return self.head(h)
+
+    return Net().to(dev)
+
+
+def _worker(rank, world, port, q, case, level, graphed):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     import sys
     from datetime import timedelta
     import torch.distributed as dist
-    import torch.nn as nn
     import torch.nn.functional as F
     sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
                                     "adaptive-precision-ascension_b200"))
@@ -46,19 +82,20 @@ def _worker(rank, world, port, q, level, graphed):
     try:
         from apa import APAConfig, APALinear, APAManager
         out = {}
+        tokens = 8192 if case == "split" else 256
+        d = 1024 if case == "split" else 2048
         for nvls in (True, False):
             cfg = APAConfig(device=str(dev), check_interval=4)
             torch.manual_seed(0)
-            model = nn.Sequential(APALinear(2048, 2048, config=cfg), nn.ReLU(),
-                                  APALinear(2048, 16, config=cfg)).to(dev)
-            for m in model:
+            model = _model(case, cfg, dev, rank)
+            for m in model.modules():
                 if isinstance(m, APALinear):
                     m.level = level
             mgr = APAManager(model, cfg, dp_nvls=nvls)
             opt = torch.optim.AdamW(mgr.get_trainable_parameters(), lr=1e-3)
             g = torch.Generator().manual_seed(100 + rank)
-            xs = torch.empty(256, 2048, device=dev)
-            ys = torch.empty(256, dtype=torch.long, device=dev)
+            xs = torch.empty(tokens, d, device=dev)
+            ys = torch.empty(tokens, dtype=torch.long, device=dev)
             gstep = None
             if graphed:
                 from apa.graphs import GraphedTrainStep
@@ -66,8 +103,8 @@ def _worker(rank, world, port, q, level, graphed):
                                          warmup=2, static_inputs=True)
             keeps = []
             for step in range(STEPS):
-                xs.copy_(torch.randn(256, 2048, generator=g))
-                ys.copy_(torch.randint(0, 16, (256,), generator=g))
+                xs.copy_(torch.randn(tokens, d, generator=g))
+                ys.copy_(torch.randint(0, 16, (tokens,), generator=g))
                 if gstep is not None:
                     _, keep = gstep(xs, ys)
                 else:
@@ -80,15 +117,16 @@ def _worker(rank, world, port, q, level, graphed):
                 keeps.append(bool(keep))
             torch.cuda.synchronize()
             gstep = None
-            used = mgr._dp.nvls is not None
-            out[nvls] = dict(used=used, keeps=keeps,
+            nv = mgr._dp.nvls
+            out[nvls] = dict(used=nv is not None, fused=nv.fused_calls if nv else 0,
+                             standalone=nv.standalone_calls if nv else 0, keeps=keeps,
                              w=[p.detach().double().cpu() for p in mgr.get_trainable_parameters()])
             del mgr, opt, model
             torch.cuda.synchronize()
         from apa import _lib
         status = _lib.device_status()
-        q.put((rank, {k: dict(used=v["used"], keeps=v["keeps"], sums=[float(w.sum()) for w in v["w"]],
-                              abs=[float(w.abs().sum()) for w in v["w"]],
+        q.put((rank, {k: dict(used=v["used"], fused=v["fused"], standalone=v["standalone"], keeps=v["keeps"],
+                              sums=[float(w.sum()) for w in v["w"]], abs=[float(w.abs().sum()) for w in v["w"]],
                               maxdiff=[float((a - b).abs().max()) for a, b in zip(v["w"], out[False]["w"])])
                       for k, v in out.items()}, status))
     except Exception as e:   # report, then leave the group normally
@@ -97,12 +135,12 @@ def _worker(rank, world, port, q, level, graphed):
         dist.destroy_process_group()
 
 
-def _run(level, graphed, world=2):
+def _run(case, level, graphed, world=2):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, level, graphed)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, case, level, graphed)) for r in range(world)]
     for p in procs:
         p.start()
     res = dict((r[0], r[1:]) for r in (q.get(timeout=300) for _ in procs))
@@ -114,11 +152,14 @@ def _run(level, graphed, world=2):
     return res
 
 
+CASES = [("fused", 0, False), ("fused", 0, True), ("fused", 1, False), ("fused", 1, True), ("fused", 2, False),
+         ("fused", 2, True), ("split", 0, False), ("split", 0, True), ("split", 2, False), ("unused", 0, False)]
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("graphed", [False, True])
-@pytest.mark.parametrize("level", [0, 1, 2])
-def test_nvls_average_matches_nccl(level, graphed):
-    res = _run(level, graphed)
+@pytest.mark.parametrize("case,level,graphed", CASES)
+def test_nvls_average_matches_nccl(case, level, graphed):
+    res = _run(case, level, graphed)
     out0, status0 = res[0]
     if not out0[True]["used"]:
         pytest.skip("no NVLink multicast on these GPUs: the NCCL buckets carry every gradient")
@@ -134,3 +175,9 @@ def test_nvls_average_matches_nccl(level, graphed):
             assert max(out[True]["maxdiff"]) == 0.0      # exact sums of E4M3 gradients
         else:
             assert max(out[True]["maxdiff"]) < 1e-5
+        if not graphed:
+            # the GEMM's epilogue reduced the large gradients, except where
+            # the layer did not run on this rank (standalone zeros)
+            assert out[True]["fused"] > 0
+            if case == "unused" and r == 1:
+                assert out[True]["standalone"] > 0
