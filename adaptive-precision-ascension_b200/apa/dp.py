@@ -111,16 +111,15 @@ class _NvlsGradients:
     apa_dp_region_reduce on the side stream). A one-thread apa_dp_region_wait
     on the side stream marks the gradient complete; the step's later work
     joins that stream. No kernel on the main stream waits long for another
-    rank, so ranks whose backward passes differ (a layer one rank skipped
-    gets its zeros at the end of that rank's backward) cannot block each
-    other. Per GPU and gradient
+    rank. Per GPU and gradient
     of B bytes about B crosses NVLink each way whatever the number of ranks,
     against 2 (world - 1) / world B for a ring all-reduce.
 
-    Every rank must reduce these gradients in every step: a rank whose layer
-    produced no gradient contributes zeros (finish() launches its reduction);
-    a rank that skips the step altogether makes the others' bounded waits
-    expire, which the next ladder decision reports as an error."""
+    Every rank must produce and reduce these gradients in every step: a rank
+    that did not run one of these layers raises at the end of its backward
+    (GradientAverager.issue_remaining); a rank that skips the step altogether
+    makes the others' bounded waits expire, which the next ladder decision
+    reports as an error."""
 
     def __init__(self, params, pg, world: int, rank: int, device, ctas: int):
         import torch.distributed._symmetric_memory as symm
@@ -336,7 +335,6 @@ class GradientAverager:
         pin = device.type == "cuda"
         self._mask_host = torch.zeros(max(1, len(self.order)), dtype=torch.int32, pin_memory=pin)
         self._ready = set()            # ids of parameters marked ready in this step
-        self._zeroed = set()
         self.accumulating = False      # inside no_sync(): gradients accumulate, nothing is reduced
         self.next = 0
         self.armed = False
@@ -393,7 +391,6 @@ class GradientAverager:
         self.ready_count = 0
         self.launch_marks = []
         self._ready = set()
-        self._zeroed = set()           # NVLS gradients this rank contributed zeros for
         self.armed = True
 
     @contextlib.contextmanager
@@ -586,23 +583,22 @@ class GradientAverager:
             self.limited = False
 
     def issue_remaining(self):
-        """Issue every bucket not yet issued, in order (asynchronous). NVLS
-        gradients this rank produced none of are contributed as zeros first:
-        the other ranks' weight-gradient GEMMs wait for this rank's regions,
-        so the contribution must be queued before any other collective of the
-        step (the telemetry all-reduce, the remaining buckets)."""
+        """Issue every bucket not yet issued, in order (asynchronous). Every
+        rank must produce every NVLS gradient in every step (the ranks'
+        weight-gradient kernels average them region by region with each
+        other); a rank that produced none of one raises here, before any other
+        collective of the step: models whose layers differ between ranks use
+        the NCCL buckets (dp_nvls=False, the default), which reduce a missing
+        gradient as zeros."""
         if self.graphed:
             return
-        if self.nvls is not None:
-            dev = self.nvls.buf.device
-            for p in self.nvls.params:
-                if id(p) not in self._ready and id(p) not in self._zeroed:
-                    v = self.nvls.views[id(p)]
-                    v.zero_()
-                    if p.grad is None or p.grad.data_ptr() != v.data_ptr():
-                        p.grad = v
-                    self._zeroed.add(id(p))
-                    self.nvls.reduce(p)
+        if self.nvls is not None and not self.accumulating:
+            missing = [p for p in self.nvls.params if id(p) not in self._ready]
+            if missing:
+                raise RuntimeError(
+                    f"data parallel (dp_nvls=True): {len(missing)} NVLS weight gradient(s) were not produced on this "
+                    "rank in this step; every rank must run every APALinear of the NVLS path in every step "
+                    "(use dp_nvls=False for models whose layers differ between ranks)")
         while self.next < len(self.buckets):
             self._launch(self.buckets[self.next])
             self.next += 1
