@@ -393,3 +393,64 @@ def test_mixed_dtypes_unused_and_accumulation_two_ranks():
     a0 = torch.tensor(out[0]["accum_a"])
     want = (torch.tensor(out[0]["local_accum_a"]) + torch.tensor(out[1]["local_accum_a"])) / 2
     assert torch.equal(a0, torch.tensor(out[1]["accum_a"])) and torch.allclose(a0, want, atol=1e-5)
+
+
+class _FakeNvls:
+    """Stands in for the NVLS gradient buffer (which needs CUDA symmetric
+    memory): the host-side bookkeeping GradientAverager keeps for it."""
+
+    def __init__(self, params):
+        self.params = list(params)
+        self.index = {id(p): i for i, p in enumerate(self.params)}
+        self.views = {id(p): torch.zeros_like(p) for p in self.params}
+        self.fused_now = set()
+        self.reduced = []
+
+    def step_begin(self):
+        self.fused_now.clear()
+
+    def reduce(self, p):
+        self.reduced.append(id(p))
+
+    def join(self, stream):
+        pass
+
+
+def _nvls_missing_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from apa.dp import GradientAverager
+        torch.manual_seed(0)
+        model = nn.Linear(8, 8, bias=False)
+        avg = GradientAverager(_FakeManager(model), None)
+        avg.nvls = _FakeNvls([model.weight])
+        avg.buckets, avg.next = [], 0       # only the NVLS gradient: no collective in this test
+        out = {}
+        avg.arm()
+        if rank == 0:
+            avg._ready.add(id(model.weight))   # this rank's backward produced it
+        try:
+            avg.issue_remaining()
+            out["raised"] = None
+        except RuntimeError as e:
+            out["raised"] = str(e)
+        # inside no_sync the gradients are not reduced yet: nothing is checked
+        avg.arm()
+        with avg.no_sync():
+            avg.issue_remaining()
+        out["no_sync_ok"] = True
+        q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_nvls_gradient_missing_on_a_rank_raises():
+    """With the NVLS path every rank must produce every NVLS gradient in every
+    step (the ranks' kernels average them region by region); a rank that did
+    not raises at the end of its backward, before issuing any collective."""
+    out = _run_two(_nvls_missing_worker)
+    assert out[0]["raised"] is None
+    assert out[1]["raised"] is not None and "dp_nvls=False" in out[1]["raised"]
+    assert out[0]["no_sync_ok"] and out[1]["no_sync_ok"]
