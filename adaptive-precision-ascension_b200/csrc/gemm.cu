@@ -1068,7 +1068,7 @@ __global__ void __launch_bounds__(threads_for<EW>(), 1)
             if (col0 >= ea.N) break;
             const int64_t g = (int64_t)rb * ncb + col0 / dpr::kRegionCols;
             if ((int)(g % ea.dp.world) == ea.dp.rank)
-              dpr::reduce_region(ea.dp, rb, col0 / dpr::kRegionCols, dp_epoch, lane, /*defer=*/true);
+              dpr::reduce_region(ea.dp, rb, col0 / dpr::kRegionCols, dp_epoch, lane);
           }
         }
       }
