@@ -104,14 +104,12 @@ class _NvlsGradients:
     owner rank (multimem.ld_reduce through the switch, multimem.st of the
     mean to every rank). The weight-gradient GEMM does it in its epilogue
     (apa_linear_wgrad_dp: every region published as soon as it is stored,
-    the owned ones averaged while the tensor cores compute later tiles, and
-    any region whose contributions were not in within a few microseconds left
-    to apa_dp_region_reduce on a side stream); gradients written otherwise
-    take the standalone kernels (apa_dp_region_signal, then
-    apa_dp_region_reduce on the side stream). A one-thread apa_dp_region_wait
-    on the side stream marks the gradient complete; the step's later work
-    joins that stream. No kernel on the main stream waits long for another
-    rank. Per GPU and gradient
+    the owned ones averaged while the tensor cores compute later tiles; a
+    gradient the plan splits along the tokens leaves its owned regions to
+    apa_dp_region_reduce on a side stream); gradients written otherwise take
+    the standalone kernels (apa_dp_region_signal, then apa_dp_region_reduce
+    on the side stream). A one-thread apa_dp_region_wait on the side stream
+    marks the gradient complete; the step's later work joins that stream. Per GPU and gradient
     of B bytes about B crosses NVLink each way whatever the number of ranks,
     against 2 (world - 1) / world B for a ring all-reduce.
 
@@ -198,8 +196,8 @@ class _NvlsGradients:
 
     def queued(self, p) -> None:
         """p's weight-gradient GEMM (apa_linear_wgrad_dp) is queued on the
-        current stream: the regions its epilogue deferred, then the
-        completion wait, go on the side stream."""
+        current stream: the regions it left to the side stream (split
+        gradients), then the completion wait, go on the side stream."""
         from . import _lib
         self.fused_now.add(id(p))
         self.fused_calls += 1

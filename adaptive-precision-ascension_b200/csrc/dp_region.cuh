@@ -16,17 +16,15 @@
 //
 // The weight-gradient GEMM runs the protocol in its epilogue (the reduction
 // of finished regions overlaps the MMAs of later tiles); dp_nvls.cu has the
-// same protocol as a standalone kernel for gradients written some other way.
-// A kernel on the ranks' main streams never waits long for another rank: the
-// GEMM's epilogue gives an owned region at most kEpilogueWaitNs, and a region
-// whose contributions are not all in by then is marked deferred (a local word
-// per region, tagged with the launch) and left to the standalone kernel,
-// which a side stream runs after the GEMM with the full bound. So no wait of
-// one rank's main stream can depend on work queued behind another rank's
-// (a rank contributing zeros for a layer it did not run, at the end of its
-// backward, cannot close a cycle). Every long wait is bounded (2 s); on
-// expiry the waiter sets a status bit and still signals, so the other ranks'
-// waits end.
+// same protocol as standalone kernels for gradients written some other way
+// (a gradient split along the tokens marks its owned regions deferred, a
+// local word per region tagged with the launch, for the standalone kernel a
+// side stream runs after it). Every rank runs the same GEMMs in the same
+// order, and every warp signals a tile's regions before it waits for any of
+// them, so no wait depends on work queued behind another wait (every rank
+// must produce every such gradient in every step; the host checks). Every
+// wait is bounded (2 s); on expiry the waiter sets a status bit and still
+// signals, so the other ranks' waits end, and later waits give up at once.
 #pragma once
 
 #include "apa_common.cuh"
@@ -38,7 +36,6 @@ constexpr int kRegionRows = 32;
 constexpr int kRegionCols = 64;
 constexpr unsigned int kStatusTimeoutReady = 1u << 12;   // a region's contributions did not all arrive
 constexpr unsigned int kStatusTimeoutDone = 1u << 13;    // the gradient's regions were not all reduced
-constexpr unsigned long long kEpilogueWaitNs = 10000ull;   // an epilogue's wait before it defers a region
 
 // The gradient and its counters (all nullable when the reduction is off).
 struct RegionArgs {
@@ -49,7 +46,7 @@ struct RegionArgs {
   const unsigned int* ready;       // the same counters, this rank's copy
   unsigned int* done_mc;           // regions reduced, multicast
   const unsigned int* epoch;       // this rank's launch count for this gradient
-  unsigned int* deferred;          // per region, this rank's copy: epoch + 1 when deferred in that launch
+  unsigned int* deferred;          // per region, this rank's copy: epoch + 1 when left to the side stream
   int world, rank;
   float scale;                     // 1 / world
 };
@@ -108,37 +105,17 @@ __device__ __forceinline__ bool wait_at_least(const unsigned int* p, unsigned in
   return true;
 }
 
-// One thread: whether *p reaches target within `ns` (no status on expiry).
-__device__ __forceinline__ bool reaches_within(const unsigned int* p, unsigned int target, unsigned long long ns) {
-  if ((int)(ld_acquire_sys(p) - target) >= 0) return true;
-  const unsigned long long t0 = global_ns();
-  while ((int)(ld_acquire_sys(p) - target) < 0)
-    if (global_ns() - t0 > ns) return false;
-  return true;
-}
 
 // One thread, after this rank's values of region g are globally visible.
 __device__ __forceinline__ void signal_ready(const RegionArgs& a, int64_t g) { red_add_release(a.ready_mc + g, 1u); }
 
 // One warp, owner of region (rb, cb) in launch `epoch`: wait for every
-// rank's values, average the region across ranks, tell every rank. With
-// `defer` (the GEMM's epilogue) the wait is short, and a region not ready by
-// then is marked deferred and left for the standalone kernel.
-__device__ __forceinline__ void reduce_region(const RegionArgs& a, int rb, int cb, unsigned int epoch, int lane,
-                                              bool defer = false) {
+// rank's values, average the region across ranks, tell every rank.
+__device__ __forceinline__ void reduce_region(const RegionArgs& a, int rb, int cb, unsigned int epoch, int lane) {
   const int64_t g = (int64_t)rb * region_cols(a.cols) + cb;
-  const unsigned int target = (unsigned int)a.world * (epoch + 1u);
   int ok = 1;
-  if (defer) {
-    if (lane == 0) {
-      ok = reaches_within(a.ready + g, target, kEpilogueWaitNs) ? 1 : 0;
-      if (!ok) a.deferred[g] = epoch + 1u;
-    }
-    if (__shfl_sync(0xFFFFFFFFu, ok, 0) == 0) return;
-  } else {
-    if (lane == 0) ok = wait_at_least(a.ready + g, target, kStatusTimeoutReady) ? 1 : 0;
-    ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-  }
+  if (lane == 0) ok = wait_at_least(a.ready + g, (unsigned int)a.world * (epoch + 1u), kStatusTimeoutReady) ? 1 : 0;
+  ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
   fence_sys();
   if (ok) {
     // half a warp per row: 16 lanes x 4 columns = the region's 64 columns;

@@ -325,16 +325,15 @@ int apa_bias_grad_noalloc(const void* dy, int dy_dtype, int64_t rows, int64_t co
  * rank:
  *   either apa_linear_wgrad_dp (the GEMM runs the protocol in its epilogue)
  *     and, on a side stream after it, apa_dp_region_reduce with
- *     only_deferred = 1 (the regions the epilogue did not find ready within
- *     a few microseconds),
+ *     only_deferred = 1 (the regions a split gradient left to it),
  *   or, after the gradient is written some other way, apa_dp_region_signal on
  *     the stream that wrote it and apa_dp_region_reduce (only_deferred = 0)
  *     after it;
  *   then apa_dp_region_wait: waits until every region is averaged (done
  *     reaches regions x (epoch + 1)), then advances the epoch; work queued
  *     after it sees the mean over ranks in every rank's gradient.
- * Only apa_dp_region_reduce and apa_dp_region_wait wait long for other ranks,
- * so a rank's main stream never does. Those waits are bounded (2 s); on
+ * Every rank must run the same gradients in the same order (each waits in
+ * its GEMM's epilogue for the others' regions). Waits are bounded (2 s); on
  * expiry the library status word is set (see apa_get_device_status; the
  * ladder's decision record reports it), the waiter still signals, later
  * waits give up at once, and the kernels return. Ranks may mix the two forms.
@@ -357,9 +356,7 @@ int apa_dp_region_wait(const unsigned int* done_local, unsigned int* epoch_local
  * counters and ratio_max of this rank's gradient), then every 32 x 64 region
  * of it, as soon as this rank's values are stored, published to the other
  * ranks, and the regions this rank owns averaged through the switch by the
- * same epilogue warps while the tensor cores compute later tiles (a region
- * whose contributions are not all in within a few microseconds is deferred
- * to the side stream's apa_dp_region_reduce pass). dw_mc is the multicast
+ * same epilogue warps while the tensor cores compute later tiles. dw_mc is the multicast
  * address of dw; the counters as for apa_dp_region_*. Work that reads dw
  * queues after apa_dp_region_wait. Shapes whose weight gradient is split
  * along the tokens take the split kernels, then publish every region and
