@@ -1,13 +1,13 @@
 // Data-parallel averaging of weight gradients through NVLink SHARP (NVLS),
 // standalone form of the region protocol of dp_region.cuh, for gradients the
-// weight-gradient GEMM did not reduce in its epilogue (split-K plans, a rank
-// whose layer produced no gradient this step, accumulated gradients):
+// weight-gradient GEMM did not reduce in its epilogue (split-K plans,
+// accumulated gradients):
 //
 //   apa_dp_region_signal   after the gradient is written: publish every
 //                          region of this rank (one multimem.red each)
 //   apa_dp_region_reduce   a few CTAs: average the regions this rank owns
 //                          (waits for every rank's signal, ld_reduce, st),
-//                          or only those a GEMM epilogue deferred
+//                          or only those a split gradient left to it
 //   apa_dp_region_wait     one thread: wait until every region of the
 //                          gradient has been averaged, then advance the epoch
 //
