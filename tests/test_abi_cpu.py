@@ -110,3 +110,33 @@ def test_new_entry_points_validate_without_gpu():
     assert lib.apa_adamw_cast(16, 16, 16, 16, 4, 8, 4, 1e-3, 0.9, 0.999, 1e-8, 0.0, 1, 16, 3, 16, None, 0, None,
                               None) == _lib.ERR_INVALID
     assert lib.apa_tensor_stats(None, 0, 10, 16, None) == _lib.ERR_INVALID
+
+
+def test_region_protocol_entry_points_without_gpu():
+    """The data-parallel region entry points count regions and reject bad
+    arguments before any CUDA call (32 x 64 regions; cols and the row pitch
+    multiples of 4; world 2..64)."""
+    from apa import _lib
+    if not os.path.exists(_lib.LIB_PATH):
+        pytest.skip("library not built")
+    lib = _lib.lib()
+    n = ctypes.c_int64(0)
+    for rows, cols, want in ((32, 64, 1), (33, 65, 4), (4096, 4096, 128 * 64), (1, 4, 1)):
+        assert lib.apa_dp_regions(rows, cols, ctypes.addressof(n)) == _lib.OK
+        assert n.value == want, (rows, cols)
+    assert lib.apa_dp_regions(0, 64, ctypes.addressof(n)) == _lib.ERR_INVALID
+    assert lib.apa_dp_regions(64, 64, None) == _lib.ERR_INVALID
+    fake = 1 << 20   # never dereferenced: validation fails first
+    common = (fake, fake, fake, fake, fake)   # ready local, ready mc, done mc, epoch, deferred
+    # missing pointer, world 1, rank out of range, cols not a multiple of 4
+    assert lib.apa_dp_region_signal(None, 64, 32, 64, *common, 2, 0, None) == _lib.ERR_INVALID
+    assert lib.apa_dp_region_signal(fake, 64, 32, 64, *common, 1, 0, None) == _lib.ERR_INVALID
+    assert lib.apa_dp_region_signal(fake, 64, 32, 64, *common, 2, 2, None) == _lib.ERR_INVALID
+    assert lib.apa_dp_region_signal(fake, 66, 32, 66, *common, 2, 0, None) == _lib.ERR_ALIGN
+    assert lib.apa_dp_region_reduce(fake, 64, 32, 64, *common, 2, 0, 2, 4, None) == _lib.ERR_INVALID
+    assert lib.apa_dp_region_reduce(fake, 64, 32, 64, *common, 2, 0, 0, 0, None) == _lib.ERR_INVALID
+    assert lib.apa_dp_region_wait(None, fake, 4, None) == _lib.ERR_INVALID
+    assert lib.apa_dp_region_wait(fake, fake, 0, None) == _lib.ERR_INVALID
+    assert lib.apa_linear_wgrad_dp(0, None, 64, None, 64, None, 64, 64, 64, 64, None, None, None, 0,
+                                   fake, *common[:4], fake, 2, 0, None) == _lib.ERR_INVALID
+    assert lib.apa_set_pdl(2) == _lib.ERR_INVALID
